@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""W4A4 linear benchmark on B200 (Llama-2-7B linear shapes).
+
+One step = the seven W4A4 linears of one Llama-2-7B decoder layer at M tokens
+(q, k, v, o: 4096 -> 4096; gate, up: 4096 -> 11008; down: 11008 -> 4096 with the
+172 x 64 Hadamard-product rotation), each one fused rotate+quantize of its
+input (shared by q/k/v and by gate/up) plus one tcgen05 W4A4 GEMM with the
+dequant epilogue: 4 + 7 kernel launches. Metric: W4A4 linear TOPS
+(2*M*N*K integer ops per linear) over the whole step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (under torchrun): every rank runs the same layer on its own token batch
+(data parallel over tokens, no collective on the data path), weak scaling;
+elapsed time is the max over ranks. `--impl reference` times the CPU W4A4
+linear of the oracle restatement (the reference's own path is PyTorch CPU
+fake-quant; its arithmetic is restated in oracle/) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYER = [("q", 4096, 4096), ("k", 4096, 4096), ("v", 4096, 4096), ("o", 4096, 4096),
+         ("gate", 4096, 11008), ("up", 4096, 11008), ("down", 11008, 4096)]
+# which quantised input each linear consumes (q/k/v share one, gate/up share one)
+INPUT_OF = {"q": "attn", "k": "attn", "v": "attn", "o": "o", "gate": "mlp", "up": "mlp", "down": "down"}
+INPUT_K = {"attn": 4096, "o": 4096, "mlp": 4096, "down": 11008}
+METRIC = "W4A4 linear TOPS at Llama-2-7B shapes (M=1..2048), % of int8 TC peak"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--tokens", type=int, default=2048)
+    p.add_argument("--replicas", type=int, default=4, help="layer replicas cycled so the working set exceeds L2")
+    p.add_argument("--no-sweep", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    return p.parse_args()
+
+
+def layer_ops(M: int) -> float:
+    return float(sum(2 * M * n * k for _, k, n in LAYER))
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return {"hbm_gbs": float(pk["hbm_gbs"]), "bf16_tflops": float(pk["bf16_tflops"]),
+                "bf16_tflops_sustained": float(pk.get("bf16_tflops_sustained", pk["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, gpu_index: int):
+        self.samples = []
+        self.window = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(gpu_index), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def mark(self, t0, t1):
+        self.window = (t0, t1)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for t, line in self.samples:
+            if self.window and not (self.window[0] - 0.15 <= t <= self.window[1] + 0.15):
+                continue
+            parts = [s.strip() for s in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            rows = [[s.strip() for s in line.split(",")] for _, line in self.samples[-3:]]
+            rows = [r for r in rows if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = sorted({self.NAMES[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- reference arm / CPU baseline
+def cpu_layer_sample(rows: int, seed: int = 0):
+    """Prepares the oracle's CPU W4A4 layer on `rows` tokens (weights pre-packed, as the GPU path)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle
+
+    from dscquant_b200 import synthetic
+
+    f32 = lambda b: (b.astype(np.uint32) << 16).view(np.float32)  # noqa: E731
+    layers = []
+    for i, (name, K, N) in enumerate(LAYER):
+        w = synthetic.weights_bf16(N, K, seed=1000 + i)
+        wr = oracle.rotate_c(f32(w))
+        q = oracle.quant_rows(wr, oracle.WEIGHT_SYM, 1.0, KP=K)
+        x = synthetic.activations_bf16(rows, K, seed=2000 + i)
+        layers.append((x, q["packed"], q["scales"], N))
+
+    def step():
+        for x, wp, sw, N in layers:
+            oracle.w4a4_linear(x, wp, sw, N)
+
+    return step, oracle.num_threads()
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    rows = 16
+    step, cores = cpu_layer_sample(rows)
+    for _ in range(max(args.warmup, 0)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    tops = layer_ops(rows) / dt / 1e12
+    sample = (f"{rows} of {args.tokens} tokens per step through all 7 Llama-2-7B layer linears "
+              "(CPU W4A4: Hadamard rotation, symmetric int4 codes, int32 GEMM on pre-packed int4 weights, epilogue)")
+    line = {"impl": "reference", "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4 x int4 -> int32",
+            "data": "synthetic (seeded N(0,1) activations with 1% x20 outlier channels, N(0,0.02) weights)",
+            "config": {"workload": "llama2-7b-layer-linears", "tokens": rows, "shapes_KxN": [[k, n] for _, k, n in LAYER]},
+            "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = world > 1 and "RANK" in os.environ
+    if args.impl == "reference":
+        if dist:
+            pass  # other ranks exit without work
+        run_reference(args, rank, world)
+        return
+
+    import numpy as np
+    import torch
+
+    import dscquant_b200 as dq
+    from dscquant_b200 import _lib, ops, synthetic
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if dist:
+        import datetime
+
+        import torch.distributed as tdist
+
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = tdist
+    _lib.load()
+    peaks = load_peaks()
+    M, R = args.tokens, args.replicas
+
+    # ---- model state: R replicas of one layer's weights (packed once) and inputs
+    def bf(bits):
+        return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).to(dev)
+
+    reps = []
+    for r in range(R):
+        mods = {}
+        for i, (name, K, N) in enumerate(LAYER):
+            base = torch.nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=dev)
+            with torch.no_grad():
+                base.weight.copy_(bf(synthetic.weights_bf16(N, K, seed=1000 + i + 17 * r)))
+            ql = dq.QuantLinear(base, dq.QuantConfig())
+            ql.enabled = True
+            ql.prepare()
+            ql.base.weight.data = torch.empty(0, device=dev, dtype=torch.bfloat16)  # only packed weights stay
+            mods[name] = ql
+        xs = {k: bf(synthetic.activations_bf16(M, K, seed=3000 + 31 * r + K + rank)) for k, K in INPUT_K.items()}
+        reps.append((mods, xs))
+    outs = {name: torch.empty((M, N), dtype=torch.bfloat16, device=dev) for name, _, N in LAYER}
+
+    stream = torch.cuda.current_stream(dev)
+    gemm_events = []  # (start, end, ops) of GEMM launches in the timed region
+    quant_events = []  # (start, end, bytes)
+
+    def step(i, record=False):
+        mods, xs = reps[i % R]
+        qs = {}
+        for key, K in INPUT_K.items():
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            qs[key] = ops.rowquant(xs[key], "act_sym", rotate=True, KP=K)
+            if record:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record(stream)
+                quant_events.append((e0, e1, M * K * 2 + M * K // 2 + 4 * M))
+        for name, K, N in LAYER:
+            ql = mods[name]
+            q = qs[INPUT_OF[name]]
+            p = ql._prep
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            rc = _lib.load().dscq_matmul(ops._ptr(q.packed), ops._ptr(p["packed"]), ops._ptr(q.scales), None,
+                                         ops._ptr(p["sw"]), None, None, None, M, N, K, _lib.BF16,
+                                         ops._ptr(outs[name]), None, 0, ops._stream(dev))
+            _lib.check(rc, "matmul")
+            if record:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record(stream)
+                gemm_events.append((e0, e1, 2.0 * M * N * K))
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    sampler = ClockSampler(local)
+    time.sleep(0.3)
+    barrier()
+    t_start = time.time()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i, record=True)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_end = time.time()
+    barrier()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    sampler.mark(t_start, t_end)
+    clocks = sampler.stop()
+    if pg is not None:
+        t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = layer_ops(M) * world / (ms_per_step * 1e-3) / 1e12
+
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in gemm_events)
+    gemm_ops = sum(o for _, _, o in gemm_events)
+    quant_ms = sum(a.elapsed_time(b) for a, b, _ in quant_events)
+    quant_bytes = sum(o for _, _, o in quant_events)
+    gemm_tops = gemm_ops / (gemm_ms * 1e-3) / 1e12
+    quant_gbs = quant_bytes / (quant_ms * 1e-3) / 1e9
+    int8_peak = 2.0 * peaks["bf16_tflops"]  # kind::i8 issues at twice the kind::f16 rate
+
+    status = ops.device_status(dev)
+
+    # ---- e2e through the public API (QuantLinear.forward) with pinned host buffers
+    mods = reps[0][0]
+    host_in = {name: torch.empty((M, K), dtype=torch.bfloat16, pin_memory=True) for name, K, _ in LAYER}
+    host_out = {name: torch.empty((M, N), dtype=torch.bfloat16, pin_memory=True) for name, _, N in LAYER}
+    for name, K, _ in LAYER:
+        host_in[name].copy_(reps[0][1][INPUT_OF[name]].cpu())
+    dev_in = {name: torch.empty((M, K), dtype=torch.bfloat16, device=dev) for name, K, _ in LAYER}
+    h2d = sum(M * K * 2 for _, K, _ in LAYER)
+    d2h = sum(M * N * 2 for _, _, N in LAYER)
+
+    def e2e_step():
+        for name, K, N in LAYER:
+            dev_in[name].copy_(host_in[name], non_blocking=True)
+            y = mods[name](dev_in[name])
+            host_out[name].copy_(y, non_blocking=True)
+
+    e2e_steps = max(5, min(args.steps, 30))
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    a1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = a0.elapsed_time(a1) / e2e_steps
+    if pg is not None:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = layer_ops(M) * world / (e2e_ms * 1e-3) / 1e12
+
+    # ---- sweep over M for the three shapes (kernel-level, L2 flushed before each timed call)
+    sweep = []
+    if not args.no_sweep and rank == 0:
+        flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        for (K, N) in ((4096, 4096), (4096, 11008), (11008, 4096)):
+            base = torch.nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=dev)
+            with torch.no_grad():
+                base.weight.copy_(bf(synthetic.weights_bf16(N, K, seed=K + N)))
+            ql = dq.QuantLinear(base, dq.QuantConfig())
+            ql.enabled = True
+            ql.prepare()
+            for m in (1, 16, 128, 512, 2048, 8192):
+                x = bf(synthetic.activations_bf16(m, K, seed=m))
+                g_t, q_t = [], []
+                for it in range(8):
+                    flush.zero_()
+                    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                    e[0].record(stream)
+                    q = ops.rowquant(x, "act_sym", rotate=True, KP=K)
+                    e[1].record(stream)
+                    ops.w4a4_gemm(q.packed, ql._prep["packed"], q.scales, ql._prep["sw"], M=m, N=N)
+                    e[2].record(stream)
+                    torch.cuda.synchronize(dev)
+                    if it >= 2:
+                        q_t.append(e[0].elapsed_time(e[1]))
+                        g_t.append(e[1].elapsed_time(e[2]))
+                gm, qm = statistics.median(g_t), statistics.median(q_t)
+                ops_ = 2.0 * m * N * K
+                gbytes = m * K / 2 + N * K / 2 + 2 * m * N + 4 * m + 4 * N
+                sweep.append({"M": m, "K": K, "N": N, "gemm_us": round(gm * 1e3, 2), "quant_us": round(qm * 1e3, 2),
+                              "gemm_tops": round(ops_ / (gm * 1e-3) / 1e12, 1),
+                              "linear_tops": round(ops_ / ((gm + qm) * 1e-3) / 1e12, 1),
+                              "gemm_frac_int8_peak": round(ops_ / (gm * 1e-3) / 1e12 / int8_peak, 3),
+                              "gemm_frac_hbm": round(gbytes / (gm * 1e-3) / 1e9 / peaks["hbm_gbs"], 3),
+                              "quant_frac_hbm": round((m * K * 2.5 + 4 * m) / (qm * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)})
+        del flush
+
+    # ---- CPU baseline (rank 0 at N = 1)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rows = 16
+        cstep, cores = cpu_layer_sample(rows)
+        cstep()
+        n = 0
+        t0 = time.perf_counter()
+        while n < 3 or time.perf_counter() - t0 < 10.0:
+            cstep()
+            n += 1
+            if time.perf_counter() - t0 > 30.0:
+                break
+        dt = (time.perf_counter() - t0) / n
+        cpu = {"value": layer_ops(rows) / dt / 1e12, "unit": "TOPS", "cores": cores, "kind": "port",
+               "sample": f"{rows} tokens x 7 layer linears per step, {n} steps, oracle C W4A4 linear "
+                         "(rotation, symmetric int4 codes, int32 GEMM, epilogue) with pthreads"}
+
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gemm_dram_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                traffic = json.load(f).get("bytes_per_launch_at_bench_shape")
+        except Exception:
+            traffic = None
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4 x int4 -> int32 (bf16 in/out)",
+            "data": "synthetic (seeded N(0,1) activations with 1% x20 outlier channels, N(0,0.02) weights)",
+            "config": {"workload": "llama2-7b-layer-linears", "tokens_per_gpu": M,
+                       "shapes_KxN": [[k, n] for _, k, n in LAYER], "rotation": "WHT-4096 / H172xH64 (K=11008)",
+                       "activation_quant": "symmetric per-token int4", "weight_quant": "symmetric per-channel int4",
+                       "parallelism": f"dp{world} over tokens" if world > 1 else "single GPU",
+                       "l2": f"{R} layer replicas cycled (working set > 126 MB L2)"},
+            "gpu_launches": 11 * args.steps,
+            "roofline": {"kernel": "w4a4_gemm_tc", "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
+                         "unit": "TFLOP/s", "frac": gemm_tops / int8_peak, "traffic": traffic,
+                         "peak_note": f"int8 dense = 2 x {peaks['source']} bf16 cuBLAS {peaks['bf16_tflops']} TFLOP/s; "
+                                      "ops are integer ops (2 per MAC)",
+                         "share_of_step": gemm_ms / elapsed_ms},
+            "roofline_quantize": {"kernel": "rowquant", "bound": "hbm", "achieved": quant_gbs, "peak": peaks["hbm_gbs"],
+                                  "unit": "GB/s", "frac": quant_gbs / peaks["hbm_gbs"],
+                                  "share_of_step": quant_ms / elapsed_ms},
+            "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "QuantLinear.forward, pinned host input -> device -> pinned host output, per linear"},
+            "cpu_baseline": cpu, "clocks": clocks, "device_status": status, "sweep": sweep,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,360 @@
+// C ABI of the W4A4 path (include/dscq_b200.h). One translation unit so the
+// device status word is shared by every kernel of the library.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/dscq_b200.h"
+#include "gemm_w4a4.cuh"
+#include "hadamard.h"
+#include "rowquant.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+#define DSCQ_REQUIRE(cond, msg) \
+  do {                          \
+    if (!(cond)) return fail(DSCQ_ERR_INVALID, msg); \
+  } while (0)
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(DSCQ_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// sm_100 check, cached per device.
+int check_device(int* dev_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  static int cc_cache[64] = {0};
+  int cc = dev < 64 ? cc_cache[dev] : 0;
+  if (cc == 0) {
+    int major = 0, minor = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    cc = major * 10 + minor;
+    if (dev < 64) cc_cache[dev] = cc;
+  }
+  if (cc != 100)
+    return fail(DSCQ_ERR_UNSUPPORTED, "dscq_b200 kernels are built for sm_100a (B200); device " +
+                                          std::to_string(dev) + " has compute capability " + std::to_string(cc));
+  if (dev_out) *dev_out = dev;
+  return DSCQ_OK;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library has no link-time dependency on libcuda.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// u8 matrix [rows, cols] with row stride ld bytes, box [box_rows, 64 bytes].
+int make_u8_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return DSCQ_OK;
+}
+
+int g_num_sms = 0;
+
+int num_sms() {
+  if (!g_num_sms) {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_num_sms = n > 0 ? n : 148;
+  }
+  return g_num_sms;
+}
+
+template <int BN, bool SWAP, bool SPLIT>
+int launch_gemm_kernel(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq::GemmParams& gp,
+                       cudaStream_t stream) {
+  using C = dscq::GemmCfg<BN>;
+  auto kern = dscq::w4a4_gemm_tc<BN, SWAP, SPLIT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a4_gemm_tc)");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(gp.tiles_i * gp.tiles_j * gp.splits));
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (SPLIT) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(gp.splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  e = cudaLaunchKernelEx(&cfg, kern, tmP, tmQ, gp);
+  if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_tc");
+  return DSCQ_OK;
+}
+
+template <int BN, bool SWAP>
+int dispatch_split(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq::GemmParams& gp,
+                   cudaStream_t stream) {
+  return gp.splits > 1 ? launch_gemm_kernel<BN, SWAP, true>(tmP, tmQ, gp, stream)
+                       : launch_gemm_kernel<BN, SWAP, false>(tmP, tmQ, gp, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int dscq_version(void) { return 1; }
+
+const char* dscq_last_error(void) { return g_err.c_str(); }
+
+int dscq_device_status(int device, uint32_t* status, int clear) {
+  DSCQ_REQUIRE(status != nullptr, "status must not be null");
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(status, dscq::g_status, sizeof(uint32_t));
+  if (e == cudaSuccess && clear) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(dscq::g_status, &zero, sizeof(uint32_t));
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "dscq_device_status");
+  return DSCQ_OK;
+}
+
+int dscq_hadamard(int n, int8_t* out) {
+  DSCQ_REQUIRE(out != nullptr, "out must not be null");
+  if (!dscq::build_hadamard(n, out))
+    return fail(DSCQ_ERR_UNSUPPORTED, "no Hadamard construction for order " + std::to_string(n));
+  return DSCQ_OK;
+}
+
+int dscq_rotation_split(int64_t K, int* a, int* b) {
+  DSCQ_REQUIRE(a && b, "a and b must not be null");
+  int aa = 0, lb = 0;
+  if (!dscq::rotation_split(K, &aa, &lb))
+    return fail(DSCQ_ERR_UNSUPPORTED, "K=" + std::to_string(K) + " has no supported Hadamard split");
+  *a = aa;
+  *b = 1 << lb;
+  return DSCQ_OK;
+}
+
+int dscq_rowquant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x, int rotate, int rot_a,
+                  const int8_t* h_a, int mode, float clip, int64_t rows_out, int64_t KP, uint8_t* packed,
+                  int64_t ld_packed, float* scales, int32_t* zeros, int32_t* row_sums, int8_t* codes,
+                  int64_t ld_codes, void* stream) {
+  DSCQ_REQUIRE(x && packed && scales, "x, packed and scales must not be null");
+  DSCQ_REQUIRE(x_dtype == DSCQ_BF16 || x_dtype == DSCQ_F16 || x_dtype == DSCQ_F32, "x_dtype must be bf16/f16/f32");
+  DSCQ_REQUIRE(M >= 1 && M <= (1 << 24), "require 1 <= M <= 2^24");
+  DSCQ_REQUIRE(K >= 1 && K <= 32768, "require 1 <= K <= 32768");
+  DSCQ_REQUIRE(ld_x >= K, "ld_x must be >= K");
+  DSCQ_REQUIRE(rows_out >= M && rows_out <= (1 << 24), "rows_out must be >= M");
+  DSCQ_REQUIRE(KP >= K && KP % 2 == 0 && KP <= 65536, "KP must be even and >= K");
+  DSCQ_REQUIRE(ld_packed >= KP / 2, "ld_packed must be >= KP/2");
+  DSCQ_REQUIRE(mode >= DSCQ_ACT_SYM && mode <= DSCQ_ACT_ASYM_TORCH, "unknown quantizer mode");
+  DSCQ_REQUIRE(std::isfinite(clip) && clip > 0.f, "clip must be a positive finite number");
+  DSCQ_REQUIRE(!(mode == DSCQ_ACT_ASYM || mode == DSCQ_ACT_ASYM_TORCH) || zeros, "asymmetric modes need zeros");
+  DSCQ_REQUIRE(!codes || ld_codes >= KP, "ld_codes must be >= KP");
+  int log2b = 0;
+  if (rotate) {
+    int a = 0;
+    if (!dscq::rotation_split(K, &a, &log2b))
+      return fail(DSCQ_ERR_UNSUPPORTED, "K=" + std::to_string(K) + " has no supported Hadamard split");
+    DSCQ_REQUIRE(a == rot_a, "rot_a does not match the split of K (see dscq_rotation_split)");
+    DSCQ_REQUIRE(a == 1 || h_a != nullptr, "h_a must point to the a x a Hadamard factor");
+  }
+  int st = check_device(nullptr);
+  if (st) return st;
+
+  dscq::RowQuantParams p;
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.ld_x = ld_x;
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.KP = static_cast<int>(KP);
+  p.rows_out = static_cast<int>(rows_out);
+  p.rotate = rotate ? 1 : 0;
+  p.rot_a = rotate ? rot_a : 1;
+  p.log2b = log2b;
+  p.h_a = h_a;
+  p.norm = rotate ? static_cast<float>(1.0 / std::sqrt(static_cast<double>(K))) : 1.f;
+  p.mode = mode;
+  p.clip = clip;
+  p.packed = packed;
+  p.ld_packed = ld_packed;
+  p.scales = scales;
+  p.zeros = zeros;
+  p.row_sums = row_sums;
+  p.codes = codes;
+  p.ld_codes = ld_codes;
+
+  constexpr int T = 512;
+  size_t smem = static_cast<size_t>(K) * sizeof(float) * ((rotate && p.rot_a > 32) ? 2 : 1);
+  if (smem > 220 * 1024)
+    return fail(DSCQ_ERR_UNSUPPORTED, "row of K=" + std::to_string(K) + " does not fit in shared memory");
+  cudaError_t e = cudaFuncSetAttribute(dscq::rowquant_smem<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowquant)");
+  dscq::rowquant_smem<T><<<static_cast<unsigned>(rows_out), T, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch rowquant");
+  return DSCQ_OK;
+}
+
+int dscq_quantize(const void* x, int x_dtype, int64_t M, int64_t K, float clip, int fused, uint8_t* packed,
+                  float* scales, int32_t* zeros, void* stream) {
+  (void)fused;
+  DSCQ_REQUIRE(M >= 1 && M <= 65535 && K >= 1 && K <= 1048576, "Require 1<=M<=65535 and 1<=K<=1048576");
+  DSCQ_REQUIRE(clip >= 0.5f && clip <= 1.f, "Activation clip must be in [0.5,1]");
+  DSCQ_REQUIRE(zeros != nullptr, "zeros must not be null");
+  const int64_t MP = (M + 7) / 8 * 8, KP = (K + 63) / 64 * 64;
+  return dscq_rowquant(x, x_dtype, M, K, K, 0, 1, nullptr, DSCQ_ACT_ASYM, clip, MP, KP, packed, KP / 2, scales,
+                       zeros, nullptr, nullptr, 0, stream);
+}
+
+int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32_t* zx, const float* sw,
+                const int32_t* sums, const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP,
+                int out_dtype, void* out, int32_t* raw, int variant, void* stream) {
+  DSCQ_REQUIRE(a && b && sx && sw, "a, b, sx and sw must not be null");
+  DSCQ_REQUIRE(out || raw, "at least one of out / raw must be given");
+  DSCQ_REQUIRE(M > 0 && M <= (1 << 24) && N > 0 && N <= (1 << 24) && KP > 0 && KP <= 1048576 && KP % 64 == 0,
+               "Invalid dimensions (need M, N > 0 and KP a positive multiple of 64)");
+  DSCQ_REQUIRE(!zx || sums, "asymmetric activations (zx) need weight code sums");
+  DSCQ_REQUIRE(out_dtype == DSCQ_BF16 || out_dtype == DSCQ_F16 || out_dtype == DSCQ_F32, "out_dtype must be bf16/f16/f32");
+  DSCQ_REQUIRE(aligned(a, 16) && aligned(b, 16), "packed operands must be 16-byte aligned");
+  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_LARGE_M, "unknown GEMM variant");
+  int st = check_device(nullptr);
+  if (st) return st;
+
+  const int64_t kbytes = KP / 2;
+  const int kblocks = static_cast<int>((KP + 127) / 128);
+  const bool swap = variant == DSCQ_GEMM_SMALL_M || (variant == DSCQ_GEMM_AUTO && M <= 64);
+  int BN;
+  int64_t ti, tj;
+  if (swap) {
+    BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+    ti = (N + 127) / 128;
+    tj = (M + BN - 1) / BN;
+  } else {
+    const int64_t t256 = ((M + 127) / 128) * ((N + 255) / 256);
+    BN = t256 >= num_sms() ? 256 : 128;
+    ti = (M + 127) / 128;
+    tj = (N + BN - 1) / BN;
+  }
+  const int64_t tiles = ti * tj;
+  DSCQ_REQUIRE(tiles * 8 < (int64_t(1) << 31), "problem too large");
+  int splits = 1;
+  while (splits < 8 && tiles * splits * 2 <= num_sms() && kblocks >= splits * 2 * 2) splits *= 2;
+
+  CUtensorMap tmP, tmQ;
+  const uint8_t* P = swap ? b : a;
+  const uint8_t* Q = swap ? a : b;
+  const int64_t rowsP = swap ? N : M, rowsQ = swap ? M : N;
+  st = make_u8_map(&tmP, P, rowsP, kbytes, kbytes, 128);
+  if (st) return st;
+  st = make_u8_map(&tmQ, Q, rowsQ, kbytes, kbytes, BN);
+  if (st) return st;
+
+  dscq::GemmParams gp;
+  gp.M = static_cast<int>(M);
+  gp.N = static_cast<int>(N);
+  gp.kblocks = kblocks;
+  gp.tiles_i = static_cast<int>(ti);
+  gp.tiles_j = static_cast<int>(tj);
+  gp.splits = splits;
+  gp.sx = sx;
+  gp.zx = zx;
+  gp.sw = sw;
+  gp.wsum = sums;
+  gp.bias = bias;
+  gp.residual = residual;
+  gp.out = out;
+  gp.raw = raw;
+  gp.out_dtype = out_dtype;
+  gp.vec_out = (out && aligned(out, 16) && (N % 8 == 0)) ? 1 : 0;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (swap) {
+    if (BN == 16) return dispatch_split<16, true>(tmP, tmQ, gp, s);
+    if (BN == 32) return dispatch_split<32, true>(tmP, tmQ, gp, s);
+    return dispatch_split<64, true>(tmP, tmQ, gp, s);
+  }
+  if (BN == 256) return dispatch_split<256, false>(tmP, tmQ, gp, s);
+  return dispatch_split<128, false>(tmP, tmQ, gp, s);
+}
+
+int dscq_pack_int4(const int8_t* codes, int64_t rows, int64_t K, int64_t ld_codes, uint8_t* packed,
+                   int64_t ld_packed, int32_t* bad_count, void* stream) {
+  DSCQ_REQUIRE(codes && packed && bad_count, "codes, packed and bad_count must not be null");
+  DSCQ_REQUIRE(rows >= 0 && K >= 1 && ld_codes >= K && ld_packed >= (K + 1) / 2, "invalid pack_int4 shape");
+  int st = check_device(nullptr);
+  if (st) return st;
+  if (rows == 0) return DSCQ_OK;
+  const int64_t total = rows * ((K + 1) / 2);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 32));
+  dscq::pack_int4_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(codes, rows, K, ld_codes, packed,
+                                                                             ld_packed, bad_count);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch pack_int4");
+  return DSCQ_OK;
+}
+
+int dscq_unpack_int4(const uint8_t* packed, int64_t rows, int64_t ld_packed, int64_t width, int8_t* codes,
+                     int64_t ld_codes, void* stream) {
+  DSCQ_REQUIRE(codes && packed, "codes and packed must not be null");
+  DSCQ_REQUIRE(rows >= 0 && width >= 0 && ld_codes >= width && ld_packed >= (width + 1) / 2,
+               "invalid unpack_int4 shape");
+  int st = check_device(nullptr);
+  if (st) return st;
+  if (rows == 0 || width == 0) return DSCQ_OK;
+  const int64_t total = rows * width;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 32));
+  dscq::unpack_int4_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(packed, rows, ld_packed, width,
+                                                                               codes, ld_codes);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch unpack_int4");
+  return DSCQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,335 @@
+// W4A4 GEMM for sm_100a: packed-int4 operands -> TMA -> shared memory ->
+// sign-extension to int8 in the UMMA canonical 128B-swizzled layout ->
+// tcgen05.mma.kind::i8 with int32 accumulators in TMEM -> fused dequant
+// epilogue (token scale x channel scale, optional zero-point term, bias,
+// residual) -> bf16/f16/f32.
+//
+// Replaces tensor_gemm / decode_gemm / epilogue of the reference
+// (kernel/w4a4.cu:80-161): raw[m,n] = sum_k a_s4[m,k] * b_s4[n,k] in int32,
+// then out = ((raw + (8 - zx[m]) * sums[n]) * sx[m]) * sw[n] (+ bias[n]),
+// kernel/w4a4.cu:70-78. Rounding is explicit (no FMA contraction) so the
+// epilogue is reproducible bit-for-bit from the same int32 accumulators.
+//
+// Tile roles (448 threads, one CTA per SM):
+//   warps 0-3   epilogue   (warp w owns TMEM lanes 32w..32w+31 = tile rows)
+//   warp  4     TMA producer (one lane)
+//   warp  5     TMEM allocator + MMA issuer (one lane)
+//   warps 6-13  int4 -> int8 expansion (256 threads)
+// The MMA "P" operand (128 rows, TMEM lanes) is the activation tile, or the
+// weight tile when SWAP is set (small M: tokens become the MMA N dimension).
+// SPLIT splits the K loop across the CTAs of a thread-block cluster; partial
+// int32 tiles are summed through distributed shared memory by cluster rank 0.
+#pragma once
+#include "ptx.cuh"
+
+namespace dscq {
+
+enum OutDtype : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2 };
+
+struct GemmParams {
+  int M, N;              // problem size: out is [M, N]
+  int kblocks;           // number of 128-element K blocks (64 packed bytes each)
+  int tiles_i, tiles_j;  // tile grid over (P rows / 128, Q rows / BN)
+  int splits;            // K splits (= cluster size when SPLIT)
+  const float* sx;       // [M] token scales
+  const int32_t* zx;     // [M] activation zero points, or null (symmetric)
+  const float* sw;       // [N] channel scales
+  const int32_t* wsum;   // [N] weight code sums (needed when zx != null)
+  const void* bias;      // [N] out dtype, or null
+  const void* residual;  // [M, N] out dtype, or null
+  void* out;             // [M, N] out dtype, or null
+  int32_t* raw;          // [M, N] int32 accumulators, or null
+  int out_dtype;
+  int vec_out;           // 1: out rows allow 16-byte vector stores of 16-column groups
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kThreads = 448;
+  static constexpr int kExpandWarps = 8;
+  static constexpr int kExpandThreads = kExpandWarps * 32;
+  static constexpr int kRows = 128 + BN;           // P rows + Q rows per stage
+  static constexpr int kRawStage = kRows * 64;      // packed int4 bytes per stage
+  static constexpr int kExpP = 128 * 128;           // expanded int8 bytes, P
+  static constexpr int kExpStage = kRows * 128;     // expanded int8 bytes per stage
+  static constexpr int kStages = (216 * 1024) / (kRawStage + kExpStage);
+  static constexpr int kRedStride = BN + 4;         // int32 words per row of the split-K exchange tile
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr int kBarBytes = (4 * kStages + 1) * 8 + 16;
+  static constexpr int kSmemBytes = 1024 + kStages * (kRawStage + kExpStage) + kBarBytes;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16,256]");
+  static_assert(kStages >= 2, "pipeline needs two stages");
+  static_assert(128 * kRedStride * 4 <= kStages * kExpStage, "split-K exchange tile must fit in the stage buffers");
+  static_assert((kExpStage % 1024) == 0, "swizzle atoms must stay 1024-byte aligned");
+};
+
+__device__ __forceinline__ float epi_scale(int32_t acc, float s_row, float s_col) {
+  return __fmul_rn(__fmul_rn(__int2float_rn(acc), s_row), s_col);
+}
+
+__device__ __forceinline__ float load_as_float(const void* p, int64_t idx, int dtype) {
+  if (dtype == kOutBF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[idx]);
+  if (dtype == kOutF16) return __half2float(reinterpret_cast<const __half*>(p)[idx]);
+  return reinterpret_cast<const float*>(p)[idx];
+}
+
+__device__ __forceinline__ void store_from_float(void* p, int64_t idx, int dtype, float v) {
+  if (dtype == kOutBF16)
+    reinterpret_cast<__nv_bfloat16*>(p)[idx] = __float2bfloat16_rn(v);
+  else if (dtype == kOutF16)
+    reinterpret_cast<__half*>(p)[idx] = __float2half_rn(v);
+  else
+    reinterpret_cast<float*>(p)[idx] = v;
+}
+
+template <int BN, bool SWAP, bool SPLIT>
+__global__ void __launch_bounds__(448, 1)
+    w4a4_gemm_tc(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
+                 const GemmParams p) {
+  using C = GemmCfg<BN>;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* exp_base = smem;
+  uint8_t* raw_base = smem + S * C::kExpStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw_base + S * C::kRawStage);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = bars + S;
+  uint64_t* exp_full = bars + 2 * S;
+  uint64_t* exp_empty = bars + 3 * S;
+  uint64_t* tmem_full = bars + 4 * S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = SPLIT ? blockIdx.x / p.splits : blockIdx.x;
+  const int z = SPLIT ? static_cast<int>(cluster_ctarank()) : 0;
+  const int ti = tile % p.tiles_i, tj = tile / p.tiles_i;
+  const int kb0 = static_cast<int>(static_cast<int64_t>(p.kblocks) * z / p.splits);
+  const int kb1 = static_cast<int>(static_cast<int64_t>(p.kblocks) * (z + 1) / p.splits);
+  const int nkb = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], C::kExpandWarps);
+      mbar_init(&exp_full[s], C::kExpandWarps);
+      mbar_init(&exp_empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmP);
+    tma_prefetch_desc(&tmQ);
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = *tmem_slot;
+  bool tile_ok = nkb > 0;
+
+  if (warp == 4) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1u;
+        if (i >= S && !mbar_wait(&raw_empty[s], ph ^ 1u, abort_flag)) break;
+        mbar_arrive_expect_tx(&raw_full[s], C::kRawStage);
+        uint8_t* dst = raw_base + s * C::kRawStage;
+        const int kx = (kb0 + i) * 64;
+        tma_load_2d(dst, &tmP, &raw_full[s], kx, ti * 128);
+        tma_load_2d(dst + 128 * 64, &tmQ, &raw_full[s], kx, tj * BN);
+        ++issued;
+      }
+      if (*abort_flag) {
+        // Let copies already in flight land before the CTA can exit.
+        for (int j = issued > S ? issued - S : 0; j < issued; ++j) mbar_wait(&raw_full[j % S], (j / S) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_i8(128, BN);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1u;
+        if (!mbar_wait(&exp_full[s], ph, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t aP = smem_u32(exp_base + s * C::kExpStage);
+        const uint64_t da = umma_desc_sw128(aP);
+        const uint64_t db = umma_desc_sw128(aP + C::kExpP);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_i8_ss(tmem_d, da + 2 * kk, db + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&exp_empty[s]);
+      }
+      umma_commit(tmem_full);
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------ int4 -> int8 expansion
+    const int et = threadIdx.x - 6 * 32;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % S;
+      const uint32_t ph = (i / S) & 1u;
+      if (!mbar_wait(&raw_full[s], ph, abort_flag)) break;
+      if (i >= S && !mbar_wait(&exp_empty[s], ph ^ 1u, abort_flag)) break;
+      const uint8_t* src = raw_base + s * C::kRawStage;
+      uint8_t* dstP = exp_base + s * C::kExpStage;
+      for (int u = et; u < C::kRows * 4; u += C::kExpandThreads) {
+        const int row = u >> 2, c = u & 3;
+        const uint4 w = *reinterpret_cast<const uint4*>(src + u * 16);
+        uint4 o0, o1;
+        s4x8_to_s8x8(w.x, o0.x, o0.y);
+        s4x8_to_s8x8(w.y, o0.z, o0.w);
+        s4x8_to_s8x8(w.z, o1.x, o1.y);
+        s4x8_to_s8x8(w.w, o1.z, o1.w);
+        const int r = row < 128 ? row : row - 128;
+        uint8_t* rowp = (row < 128 ? dstP : dstP + C::kExpP) + r * 128;
+        const int sw = r & 7;
+        *reinterpret_cast<uint4*>(rowp + (((2 * c) ^ sw) << 4)) = o0;
+        *reinterpret_cast<uint4*>(rowp + (((2 * c + 1) ^ sw) << 4)) = o1;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&raw_empty[s]);
+        mbar_arrive(&exp_full[s]);
+      }
+    }
+  }
+
+  // ------------------------------------------------ epilogue
+  const int row_local = warp * 32 + lane;  // TMEM lane == tile row (warps 0-3)
+  const uint32_t t_row = tmem_d + (static_cast<uint32_t>(warp * 32) << 16);
+  int32_t* red = reinterpret_cast<int32_t*>(exp_base);
+  if (warp < 4) {
+    if (!mbar_wait(tmem_full, 0, abort_flag)) tile_ok = false;
+    if (*abort_flag) tile_ok = false;
+    tile_ok = __all_sync(0xffffffffu, tile_ok);
+    tc_fence_after();
+    if (SPLIT && z != 0 && tile_ok) {
+      for (int j0 = 0; j0 < BN; j0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_row + j0, r);
+        tmem_ld_wait();
+        int4* dst = reinterpret_cast<int4*>(red + row_local * C::kRedStride + j0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_int4(static_cast<int>(r[4 * q]), static_cast<int>(r[4 * q + 1]),
+                             static_cast<int>(r[4 * q + 2]), static_cast<int>(r[4 * q + 3]));
+      }
+    }
+  }
+  __syncwarp();
+  if constexpr (SPLIT) cluster_sync();
+  if (warp < 4 && (!SPLIT || z == 0) && tile_ok) {
+    const bool has_bias = p.bias != nullptr, has_res = p.residual != nullptr;
+    const bool asym = p.zx != nullptr;
+    for (int j0 = 0; j0 < BN; j0 += 16) {
+      uint32_t r[16];
+      tmem_ld16(t_row + j0, r);
+      tmem_ld_wait();
+      int32_t acc[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t) acc[t] = static_cast<int32_t>(r[t]);
+      if constexpr (SPLIT) {
+        const uint32_t local = smem_u32(red + row_local * C::kRedStride + j0);
+        for (int q = 1; q < p.splits; ++q) {
+          const uint32_t peer = dsmem_map(local, static_cast<uint32_t>(q));
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int4 x = dsmem_ld_v4(peer + 16 * v);
+            acc[4 * v] += x.x;
+            acc[4 * v + 1] += x.y;
+            acc[4 * v + 2] += x.z;
+            acc[4 * v + 3] += x.w;
+          }
+        }
+      }
+      if constexpr (!SWAP) {
+        const int m = ti * 128 + row_local;
+        const int n0 = tj * BN + j0;
+        if (m < p.M) {
+          const float sxm = p.sx[m];
+          const int32_t zc = asym ? 8 - p.zx[m] : 0;
+          const int64_t o0 = static_cast<int64_t>(m) * p.N + n0;
+          const bool full = n0 + 16 <= p.N;
+          if (p.raw) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+              if (n0 + t < p.N) p.raw[o0 + t] = acc[t];
+          }
+          if (p.out) {
+            float f[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              const int n = full ? n0 + t : min(n0 + t, p.N - 1);
+              f[t] = epi_scale(asym ? acc[t] + zc * p.wsum[n] : acc[t], sxm, p.sw[n]);
+              if (has_bias) f[t] = __fadd_rn(f[t], load_as_float(p.bias, n, p.out_dtype));
+              if (has_res) f[t] = __fadd_rn(f[t], load_as_float(p.residual, o0 + (n - n0), p.out_dtype));
+            }
+            if (full && p.vec_out && p.out_dtype == kOutBF16) {
+              uint32_t w[8];
+#pragma unroll
+              for (int t = 0; t < 8; ++t) {
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * t], f[2 * t + 1]);
+                w[t] = *reinterpret_cast<uint32_t*>(&h2);
+              }
+              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + o0);
+              dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+              dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
+#pragma unroll
+              for (int t = 0; t < 16; ++t)
+                if (n0 + t < p.N) store_from_float(p.out, o0 + t, p.out_dtype, f[t]);
+            }
+          }
+        }
+      } else {
+        const int n = ti * 128 + row_local;
+        if (n < p.N) {
+          const float swn = p.sw[n];
+          const int32_t wsn = asym ? p.wsum[n] : 0;
+          const float bn = has_bias ? load_as_float(p.bias, n, p.out_dtype) : 0.f;
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const int m = tj * BN + j0 + t;
+            if (m < p.M) {
+              const int64_t o = static_cast<int64_t>(m) * p.N + n;
+              if (p.raw) p.raw[o] = acc[t];
+              if (p.out) {
+                const int32_t corr = asym ? acc[t] + (8 - p.zx[m]) * wsn : acc[t];
+                float f = epi_scale(corr, p.sx[m], swn);
+                if (has_bias) f = __fadd_rn(f, bn);
+                if (has_res) f = __fadd_rn(f, load_as_float(p.residual, o, p.out_dtype));
+                store_from_float(p.out, o, p.out_dtype, f);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+  if constexpr (SPLIT) cluster_sync();
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    // All MMAs of this CTA must have retired before TMEM is released.
+    if (lane == 0) mbar_wait(tmem_full, 0, nullptr);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_d, C::kTmemCols);
+  }
+}
+
+}  // namespace dscq

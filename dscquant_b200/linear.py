@@ -1,0 +1,141 @@
+"""Drop-in QuantLinear (core/linear.py:8-52) running the W4A4 CUDA path.
+
+Same constructor, `enabled` flag, clip parameters and `transformed()`
+semantics as the reference. Differences, all deliberate:
+
+* the weight is rotated, quantised and packed once (`prepare()`, called
+  lazily by the first enabled forward) instead of being re-quantised on every
+  call (core/linear.py:52 requantises the full N x K weight per forward);
+  call `prepare()` again after changing the weight, the clips or the
+  interface;
+* the enabled forward runs two kernels: the fused rotate+quantize of the
+  activations and the tcgen05 W4A4 GEMM with the dequant epilogue. It accepts
+  CUDA tensors only;
+* the activation scheme follows the config: a reference-style config (only
+  `activation_bits` / `weight_bits`) gives the reference's semantics exactly
+  (asymmetric per-token codes, core/quantization.py:13-21, no online rotation);
+  `QuantConfig()` gives the symmetric per-token scheme with the online
+  Hadamard rotation applied to activations and weights.
+"""
+from __future__ import annotations
+
+import weakref
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+
+from . import ops
+
+
+@dataclass
+class QuantConfig:
+    activation_bits: int = 4
+    weight_bits: int = 4
+    activation_symmetric: bool = True   # scale = absmax/7, codes in [-8, 7]
+    online_rotation: bool = True        # y = x (H_a (x) H_b)/sqrt(K) on activations, W' = W (same) offline
+
+
+class QuantLinear(nn.Module):
+    def __init__(self, base: nn.Linear, config, interface=None, role=None, repeat=1):
+        super().__init__()
+        self.base = base
+        self.config = config
+        self.role, self.repeat = role, repeat
+        self._interface = None if interface is None else weakref.ref(interface)
+        self.weight_clip = nn.Parameter(torch.tensor(1.0, device=base.weight.device), requires_grad=False)
+        self.activation_clip = nn.Parameter(torch.tensor(1.0, device=base.weight.device), requires_grad=False)
+        self.enabled = False
+        for param in self.base.parameters():
+            param.requires_grad_(False)
+        self._prep = None
+
+    # ------------------------------------------------------------------ reference semantics
+    def transformed(self):
+        """core/linear.py:22-46: absorb the interface (per-head rotation for roles 'v'/'o', diagonal
+        scaling otherwise) into (weight, bias)."""
+        weight, bias = self.base.weight, self.base.bias
+        interface = self._interface() if self._interface else None
+        if interface is None:
+            return weight, bias
+        if hasattr(interface, "matrices"):
+            mats = interface.matrices()
+            if self.role == "v":
+                shaped = weight.float().reshape(interface.heads, interface.head_dim, -1)
+                weight = (mats.transpose(-1, -2) @ shaped).reshape_as(weight).to(weight.dtype)
+                if bias is not None:
+                    bias = (mats.transpose(-1, -2) @ bias.float().reshape(interface.heads, -1, 1)).flatten().to(
+                        bias.dtype)
+            elif self.role == "o":
+                mats = mats.repeat_interleave(self.repeat, dim=0)
+                shaped = weight.float().reshape(weight.shape[0], len(mats), interface.head_dim)
+                weight = torch.einsum("ohd,hde->ohe", shaped, mats).reshape_as(weight).to(weight.dtype)
+        else:
+            scale = interface.diagonal()
+            if self.role == "up":
+                weight = (weight.float() / scale[:, None]).to(weight.dtype)
+                if bias is not None:
+                    bias = (bias.float() / scale).to(bias.dtype)
+            else:
+                weight = (weight.float() * scale[None, :]).to(weight.dtype)
+        return weight, bias
+
+    # ------------------------------------------------------------------ W4A4 path
+    @property
+    def symmetric(self) -> bool:
+        return bool(getattr(self.config, "activation_symmetric", False))
+
+    @property
+    def rotate(self) -> bool:
+        return bool(getattr(self.config, "online_rotation", False))
+
+    def _check_bits(self) -> None:
+        if int(self.config.activation_bits) != 4 or int(self.config.weight_bits) != 4:
+            raise NotImplementedError("the CUDA path implements W4A4 only (activation_bits = weight_bits = 4)")
+
+    @torch.no_grad()
+    def prepare(self) -> None:
+        """Rotate (optionally), quantise and pack the weight once: packed [N, KP/2] u8, channel scales
+        [N] f32 and code sums [N] i32 (for the asymmetric correction, kernel/w4a4.cu:74)."""
+        self._check_bits()
+        weight, bias = self.transformed()
+        if not weight.is_cuda:
+            raise RuntimeError("QuantLinear's W4A4 path needs the weight on a CUDA device")
+        N, K = weight.shape
+        KP = (K + 63) // 64 * 64
+        w = weight if weight.dtype in (torch.bfloat16, torch.float16, torch.float32) else weight.float()
+        q = ops.rowquant(w.contiguous(), "weight_sym", clip=float(self.weight_clip), rotate=self.rotate, KP=KP,
+                         row_sums=True)
+        self._prep = dict(packed=q.packed, sw=q.scales, wsum=q.row_sums, bias=bias, K=K, N=N, KP=KP,
+                          aclip=float(self.activation_clip), bias_cache={})
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not self.enabled:
+            return self.base(x)
+        if not x.is_cuda:
+            raise RuntimeError("QuantLinear's W4A4 path runs on CUDA tensors only")
+        if x.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise RuntimeError("x must be bf16, f16 or f32")
+        if self._prep is None:
+            self.prepare()
+        p = self._prep
+        K, N = p["K"], p["N"]
+        x2 = x.reshape(-1, K)
+        if x2.stride(-1) != 1:
+            x2 = x2.contiguous()
+        mode = "act_sym" if self.symmetric else "act_asym_torch"
+        q = ops.rowquant(x2, mode, clip=p["aclip"], rotate=self.rotate, KP=p["KP"])
+        bias = None
+        if p["bias"] is not None:
+            bias = p["bias_cache"].get(x.dtype)
+            if bias is None:
+                bias = p["bias"].to(x.dtype).contiguous()
+                p["bias_cache"][x.dtype] = bias
+        y = ops.w4a4_gemm(q.packed, p["packed"], q.scales, p["sw"], M=x2.shape[0], N=N,
+                          zx=None if self.symmetric else q.zeros, sums=None if self.symmetric else p["wsum"],
+                          bias=bias, out_dtype=x.dtype)
+        return y.reshape(*x.shape[:-1], N)
+
+    def extra_repr(self) -> str:
+        return (f"in={self.base.in_features}, out={self.base.out_features}, symmetric={self.symmetric}, "
+                f"rotation={self.rotate}, enabled={self.enabled}")

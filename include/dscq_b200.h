@@ -1,0 +1,121 @@
+/*
+ * dscq_b200 -- C ABI of the B200 (sm_100a) W4A4 quantized-linear path.
+ *
+ * Plain pointers and sizes only. Every device pointer refers to memory on the
+ * current CUDA device; `stream` is a cudaStream_t (NULL = legacy default
+ * stream). All entry points are asynchronous with respect to the host unless
+ * stated otherwise and return DSCQ_OK (0) or an error code; dscq_last_error()
+ * returns a message for the last failure on the calling thread.
+ *
+ * Packed int4 layout (identical to the reference): byte j of a row holds
+ * element 2j in its low nibble and 2j+1 in its high nibble, two's complement
+ * (core/quantization.py:31-45, kernel/w4a4.cu:53).
+ */
+#ifndef DSCQ_B200_H_
+#define DSCQ_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define DSCQ_OK 0
+#define DSCQ_ERR_INVALID 1     /* bad shape, dtype, alignment or null pointer */
+#define DSCQ_ERR_CUDA 2        /* CUDA runtime error (launch, query)          */
+#define DSCQ_ERR_UNSUPPORTED 3 /* device is not sm_100 / unsupported size      */
+#define DSCQ_ERR_RANGE 4       /* value out of range (pack_int4 codes)         */
+
+/* element types */
+#define DSCQ_BF16 0
+#define DSCQ_F16 1
+#define DSCQ_F32 2
+
+/* per-row quantizer modes */
+#define DSCQ_ACT_SYM 0          /* scale = absmax*clip/7, codes in [-8, 7]                  */
+#define DSCQ_WEIGHT_SYM 1       /* core/quantization.py:7-11, codes in [-7, 7] + code sums   */
+#define DSCQ_ACT_ASYM 2         /* kernel/w4a4.cu:20-63 (rn(x/s) + zero)                     */
+#define DSCQ_ACT_ASYM_TORCH 3   /* core/quantization.py:13-21 (rn(x/s + zero))               */
+
+/* GEMM variants (dscq_matmul `variant`) */
+#define DSCQ_GEMM_AUTO 0
+#define DSCQ_GEMM_SMALL_M 1     /* weights on the 128-row MMA side, tokens as MMA N */
+#define DSCQ_GEMM_LARGE_M 2     /* activations on the 128-row MMA side              */
+
+int dscq_version(void);
+const char* dscq_last_error(void);
+
+/* Reads the sticky device status word of `device` (bit 0: a bounded wait in a
+ * kernel expired; bit 1: bad launch geometry). Synchronises the device.
+ * `clear` != 0 resets it. */
+int dscq_device_status(int device, uint32_t* status, int clear);
+
+/* Host-side +-1 Hadamard matrix of order n (row-major, n*n int8) for the
+ * orders the library constructs: 2^j, Paley I/II primes, 172. */
+int dscq_hadamard(int n, int8_t* out);
+
+/* Dense factor `a` of the Kronecker rotation H_a (x) H_(K/a) used for K. */
+int dscq_rotation_split(int64_t K, int* a, int* b);
+
+/*
+ * Replaces quantize_cuda(x, clip, fused), kernel/w4a4.cu:164-187.
+ * x [M, K] (bf16/f16/f32, row stride K). Asymmetric per-row codes exactly as
+ * the reference kernel; outputs padded like the reference:
+ *   packed [MP, KP/2] u8, scales [MP] f32, zeros [MP] i32,
+ *   MP = ceil(M/8)*8, KP = ceil(K/64)*64.
+ * `fused` is accepted for signature parity; both settings give the same bytes.
+ */
+int dscq_quantize(const void* x, int x_dtype, int64_t M, int64_t K, float clip, int fused, uint8_t* packed,
+                  float* scales, int32_t* zeros, void* stream);
+
+/*
+ * General per-row quantizer with optional online rotation (no counterpart in
+ * the reference, which absorbs rotations into weights: core/linear.py:22-46).
+ *   rotate == 0: identity. rotate != 0: y = x (H_a (x) H_b) / sqrt(K),
+ *   a from dscq_rotation_split(K) and h_a its +-1 matrix in DEVICE memory
+ *   (NULL when a == 1).
+ * mode: DSCQ_ACT_SYM / DSCQ_WEIGHT_SYM / DSCQ_ACT_ASYM / DSCQ_ACT_ASYM_TORCH.
+ * Writes rows_out (>= M) rows; KP (even, >= K) packed columns:
+ *   packed [rows_out, ld_packed >= KP/2], scales [rows_out],
+ *   zeros [rows_out] (asym modes, may be NULL otherwise),
+ *   row_sums [rows_out] (sum of codes over k < K, may be NULL),
+ *   codes [rows_out, ld_codes >= KP] int8 (may be NULL).
+ */
+int dscq_rowquant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x, int rotate, int rot_a,
+                  const int8_t* h_a, int mode, float clip, int64_t rows_out, int64_t KP, uint8_t* packed,
+                  int64_t ld_packed, float* scales, int32_t* zeros, int32_t* row_sums, int8_t* codes,
+                  int64_t ld_codes, void* stream);
+
+/*
+ * Replaces matmul_cuda(a, b, sx, zx, sw, sums, bias, M, N, fused,
+ * force_decode, fp32), kernel/w4a4.cu:189-225.
+ *   a [>= M rows, KP/2] u8 packed activations (row stride KP/2 bytes)
+ *   b [>= N rows, KP/2] u8 packed weights
+ *   sx [M] f32, sw [N] f32; zx [M] i32 + sums [N] i32 for the asymmetric
+ *   correction (both NULL for symmetric activations)
+ *   bias [N] and residual [M, N] in out_dtype, or NULL
+ *   out [M, N] out_dtype (DSCQ_BF16 / DSCQ_F16 / DSCQ_F32), or NULL
+ *   raw [M, N] i32 int32 accumulators sum_k a[m,k] b[n,k], or NULL
+ * out[m,n] = ((raw + (8 - zx[m]) sums[n]) * sx[m]) * sw[n] + bias[n] + residual[m,n]
+ * KP must be a positive multiple of 64 (as in the reference).
+ */
+int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32_t* zx, const float* sw,
+                const int32_t* sums, const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP,
+                int out_dtype, void* out, int32_t* raw, int variant, void* stream);
+
+/* pack_int4, core/quantization.py:31-40. codes [rows, K] int8 (row stride
+ * ld_codes) -> packed [rows, ceil(K/2)] (row stride ld_packed). Codes outside
+ * [-8, 7] are counted into *bad_count (device int, caller-zeroed). */
+int dscq_pack_int4(const int8_t* codes, int64_t rows, int64_t K, int64_t ld_codes, uint8_t* packed,
+                   int64_t ld_packed, int32_t* bad_count, void* stream);
+
+/* unpack_int4, core/quantization.py:42-45. */
+int dscq_unpack_int4(const uint8_t* packed, int64_t rows, int64_t ld_packed, int64_t width, int8_t* codes,
+                     int64_t ld_codes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSCQ_B200_H_ */

@@ -1,0 +1,100 @@
+"""Generates tests/golden/golden_v1.npz from the REFERENCE's own Python code.
+
+Run in a container where the reference checkout is available (its path is the
+first argument, default ../../reference relative to the repository root's
+parent). It imports core.quantization and core.linear from that checkout and
+records their outputs on seeded inputs produced by dscquant_b200.synthetic, so
+the fixtures pin both the CPU oracle (oracle/oracle.py) and the CUDA kernels to
+the reference without needing the reference at test time.
+
+    python tests/golden/make_golden.py /path/to/reference
+"""
+from __future__ import annotations
+
+import os
+import sys
+import types
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+from dscquant_b200 import synthetic  # noqa: E402
+
+
+def main(ref: str) -> None:
+    import torch
+    from torch import nn
+
+    sys.path.insert(0, ref)
+    from core import quantization as Q  # reference
+    from core.linear import QuantLinear  # reference
+
+    torch.manual_seed(0)
+    out = {"torch_version": np.array(torch.__version__)}
+
+    def bf16(bits):
+        return torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16)
+
+    def bits(t):
+        return t.detach().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    # -- quantizer functions on a ragged shape (odd K) --------------------------------
+    xq = synthetic.activations_bf16(13, 201, seed=11)
+    wq = synthetic.weights_bf16(96, 201, seed=12)
+    # crafted rows: exact .5 ties after division by the scale (amax = 7 -> scale = 1)
+    tie = np.zeros((2, 201), np.float32)
+    tie[0, :8] = [7.0, 0.5, 1.5, 2.5, -0.5, -2.5, 3.5, -6.5]
+    tie[1, :8] = [-7.0, 4.5, 5.5, 6.5, -1.5, -3.5, -4.5, 0.25]
+    wq = np.concatenate([wq, synthetic._to_bf16_bits(tie)], axis=0)
+    xq = np.concatenate([xq, synthetic._to_bf16_bits(tie)], axis=0)
+    out["q_x"] = xq
+    out["q_w"] = wq
+    for clip in (1.0, 0.75):
+        tag = str(clip).replace(".", "p")
+        code, scale = Q.weight_codes(bf16(wq), 4, clip)
+        out[f"wc_code_{tag}"] = code.to(torch.int8).numpy()
+        out[f"wc_scale_{tag}"] = scale.numpy()
+        code, scale, zero = Q.activation_codes(bf16(xq), 4, clip)
+        out[f"ac_code_{tag}"] = code.to(torch.int8).numpy()
+        out[f"ac_scale_{tag}"] = scale.numpy()
+        out[f"ac_zero_{tag}"] = zero.numpy()
+        out[f"qw_{tag}"] = bits(Q.quantize_weight(bf16(wq), 4, clip))
+        out[f"qa_{tag}"] = bits(Q.quantize_activation(bf16(xq), 4, clip))
+    codes_w = Q.weight_codes(bf16(wq), 4, 1.0)[0]
+    packed = Q.pack_int4(codes_w)
+    out["pack_codes"] = codes_w.to(torch.int8).numpy()
+    out["pack_bytes"] = packed.numpy()
+    out["unpack_codes"] = Q.unpack_int4(packed, 201).numpy()
+
+    # -- QuantLinear.forward (reference fake-quant path, as shipped) -------------------
+    cfg = types.SimpleNamespace(activation_bits=4, weight_bits=4)
+    for name, (M, K, N, bias) in {"lin_a": (16, 256, 128, True), "lin_b": (7, 320, 96, False),
+                                  "lin_cfg0": (16, 4096, 4096, False)}.items():
+        x = synthetic.activations_bf16(M, K, seed=100 + M)
+        w = synthetic.weights_bf16(N, K, seed=200 + N)
+        base = nn.Linear(K, N, bias=bias, dtype=torch.bfloat16)
+        with torch.no_grad():
+            base.weight.copy_(bf16(w))
+            if bias:
+                b = synthetic.weights_bf16(1, N, seed=300 + N, std=0.5)[0]
+                base.bias.copy_(bf16(b))
+                out[f"{name}_bias"] = b
+        ql = QuantLinear(base, cfg)
+        ql.enabled = True
+        with torch.no_grad():
+            y = ql(bf16(x))
+        out[f"{name}_shape"] = np.array([M, K, N, int(bias)])
+        out[f"{name}_y"] = bits(y)
+        if K <= 512:
+            out[f"{name}_x"] = x
+            out[f"{name}_w"] = w
+
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_v1.npz")
+    np.savez_compressed(path, **out)
+    print("wrote", path, os.path.getsize(path), "bytes")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(os.path.dirname(ROOT), "reference"))

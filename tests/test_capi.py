@@ -1,0 +1,105 @@
+"""The C-ABI library loads, exports every symbol include/dscq_b200.h declares, and its host-side logic
+(argument validation, Hadamard constructions) works without a GPU."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "dscq_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\w[\w\s\*]*?\b(dscq_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for s in ("dscq_quantize", "dscq_matmul", "dscq_rowquant", "dscq_pack_int4", "dscq_unpack_int4",
+              "dscq_hadamard", "dscq_last_error", "dscq_device_status"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(native):
+    from dscquant_b200 import _lib
+
+    for s in declared_symbols():
+        assert hasattr(native, s), s
+        assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
+    assert native.dscq_version() >= 1
+
+
+def test_hadamard_matches_oracle(native, oracle):
+    for n in (1, 8, 12, 20, 28, 172, 4096 // 64):
+        out = np.zeros((n, n), np.int8)
+        assert native.dscq_hadamard(n, out.ctypes.data_as(ctypes.c_void_p)) == 0
+        np.testing.assert_array_equal(out, oracle.hadamard(n).astype(np.int8))
+    out = np.zeros((86, 86), np.int8)
+    assert native.dscq_hadamard(86, out.ctypes.data_as(ctypes.c_void_p)) != 0
+
+
+def test_rotation_split_native(native):
+    from dscquant_b200 import ops
+
+    assert ops.rotation_split(4096) == (1, 4096)
+    assert ops.rotation_split(11008) == (172, 64)
+    assert ops.rotation_split(14336) == (28, 512)
+    assert ops.rotation_split(28672) == (28, 1024)
+    with pytest.raises(RuntimeError):
+        ops.rotation_split(3 * 5 * 7 * 11 * 13 * 17)
+
+
+def test_argument_validation_without_gpu(native):
+    from dscquant_b200 import _lib
+
+    buf = (ctypes.c_uint8 * 4096)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    # KP not a multiple of 64 -> invalid, detected before any device call
+    rc = native.dscq_matmul(p, p, p, None, p, None, None, None, 16, 16, 96, 0, p, None, 0, None)
+    assert rc == _lib.DSCQ_ERR_INVALID and "multiple of 64" in _lib.last_error()
+    # null input
+    rc = native.dscq_rowquant(None, 0, 4, 64, 64, 0, 1, None, 0, 1.0, 4, 64, p, 32, p, None, None, None, 0, None)
+    assert rc == _lib.DSCQ_ERR_INVALID
+    # reference clip range check (kernel/w4a4.cu:168)
+    rc = native.dscq_quantize(p, 0, 4, 64, 0.25, 1, p, p, p, None)
+    assert rc == _lib.DSCQ_ERR_INVALID and "clip" in _lib.last_error()
+    # asymmetric activations without weight sums
+    rc = native.dscq_matmul(p, p, p, p, p, None, None, None, 16, 16, 64, 0, p, None, 0, None)
+    assert rc == _lib.DSCQ_ERR_INVALID
+
+
+def test_valid_call_without_gpu_fails_cleanly(native):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    from dscquant_b200 import _lib
+
+    buf = (ctypes.c_uint8 * 4096)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    rc = native.dscq_rowquant(p, 0, 4, 64, 64, 0, 1, None, 0, 1.0, 4, 64, p, 32, p, None, None, None, 0, None)
+    assert rc in (_lib.DSCQ_ERR_CUDA, _lib.DSCQ_ERR_UNSUPPORTED)
+    assert _lib.last_error()
+
+
+def test_no_cpu_fallback():
+    import torch
+    from torch import nn
+
+    from dscquant_b200 import QuantConfig, QuantLinear, quantization
+
+    base = nn.Linear(64, 32, dtype=torch.bfloat16)
+    ql = QuantLinear(base, QuantConfig())
+    x = torch.randn(4, 64, dtype=torch.bfloat16)
+    torch.testing.assert_close(ql(x), base(x))  # disabled: the base layer, like the reference
+    ql.enabled = True
+    with pytest.raises(RuntimeError):
+        ql(x)
+    for fn in (lambda: quantization.weight_codes(base.weight, 4), lambda: quantization.activation_codes(x, 4),
+               lambda: quantization.pack_int4(torch.zeros(2, 2, dtype=torch.int8))):
+        with pytest.raises(RuntimeError):
+            fn()

@@ -1,0 +1,154 @@
+"""W4A4 GEMM parity on the GPU: int32 accumulators bit-exact against the oracle's packed-int4 matmul
+(kernel/w4a4.cu:123-148 restated in oracle/oracle_w4a4.c), outputs bit-exact against the oracle
+epilogue (kernel/w4a4.cu:70-78), for every kernel variant and ragged shapes; at the benchmark sizes
+through row/column checksums and sampled entries."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _packed(rng, rows, KP):
+    return rng.integers(0, 256, (rows, KP // 2), dtype=np.uint8)
+
+
+def _bf16_bits(t):
+    return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def _f32_to_bf16(f, oracle):
+    return oracle.f32_to_bf16_bits(f)
+
+
+def _run(oracle, dev, M, N, KP, variant="auto", asym=False, bias=False, residual=False, out_dtype=torch.bfloat16,
+         seed=0):
+    from dscquant_b200 import ops
+
+    rng = np.random.default_rng(seed + M * 7 + N * 13 + KP)
+    a = _packed(rng, M, KP)
+    b = _packed(rng, N, KP)
+    sx = (rng.random(M, dtype=np.float32) * 0.1 + 1e-3).astype(np.float32)
+    sw = (rng.random(N, dtype=np.float32) * 0.01 + 1e-4).astype(np.float32)
+    zx = rng.integers(0, 16, M).astype(np.int32) if asym else None
+    sums = oracle.unpack_int4(b, KP).astype(np.int64).sum(1).astype(np.int32) if asym else None
+    tb = oracle.f32_to_bf16_bits(rng.standard_normal(N).astype(np.float32)) if bias else None
+    tr = oracle.f32_to_bf16_bits(rng.standard_normal((M, N)).astype(np.float32)) if residual else None
+
+    def T(x, dt=None):
+        return None if x is None else torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+    def Tbf(bits):
+        return None if bits is None else torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(dev).to(
+            out_dtype)
+
+    out, raw = ops.w4a4_gemm(T(a), T(b), T(sx), T(sw), zx=T(zx), sums=T(sums), bias=Tbf(tb), residual=Tbf(tr),
+                             out_dtype=out_dtype, return_raw=True, variant=variant)
+    torch.cuda.synchronize()
+    ref_raw = oracle.gemm_s4(a, b, M, N, KP)
+    np.testing.assert_array_equal(raw.cpu().numpy(), ref_raw)
+    bias_f = None if tb is None else torch.from_numpy(tb.view(np.int16)).view(torch.bfloat16).to(out_dtype).float().numpy()
+    res_f = None if tr is None else torch.from_numpy(tr.view(np.int16)).view(torch.bfloat16).to(out_dtype).float().numpy()
+    ref = oracle.epilogue(ref_raw, sx, sw, zx, sums, bias_f, res_f)
+    if out_dtype == torch.bfloat16:
+        np.testing.assert_array_equal(_bf16_bits(out), oracle.f32_to_bf16_bits(ref))
+    elif out_dtype == torch.float16:
+        np.testing.assert_array_equal(out.cpu().numpy(), ref.astype(np.float16))
+    else:
+        np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
+SHAPES = [(1, 128, 128), (7, 96, 64), (9, 200, 192), (16, 4096, 4096), (33, 130, 320), (64, 256, 256),
+          (65, 300, 320), (128, 256, 1024), (200, 520, 448), (256, 512, 1024), (512, 1024, 512), (300, 1000, 2048)]
+
+
+@pytest.mark.parametrize("M,N,KP", SHAPES)
+def test_gemm_exact_auto(oracle, cuda_device, M, N, KP):
+    _run(oracle, cuda_device, M, N, KP)
+
+
+@pytest.mark.parametrize("variant", ["small_m", "large_m"])
+@pytest.mark.parametrize("M,N,KP", [(1, 128, 128), (20, 200, 256), (64, 384, 1024), (130, 260, 192), (256, 256, 4096)])
+def test_gemm_exact_forced_variant(oracle, cuda_device, variant, M, N, KP):
+    _run(oracle, cuda_device, M, N, KP, variant=variant)
+
+
+@pytest.mark.parametrize("M,N,KP", [(5, 96, 128), (100, 200, 256)])
+def test_gemm_asym_bias_residual(oracle, cuda_device, M, N, KP):
+    _run(oracle, cuda_device, M, N, KP, asym=True, bias=True, residual=True)
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.float32])
+@pytest.mark.parametrize("M", [3, 150])
+def test_gemm_out_dtypes(oracle, cuda_device, dt, M):
+    _run(oracle, cuda_device, M, 136, 192, bias=True, out_dtype=dt)
+
+
+def test_gemm_repeatable(oracle, cuda_device):
+    """Same inputs twice -> identical bits (integer accumulation, fixed epilogue order)."""
+    from dscquant_b200 import ops
+
+    rng = np.random.default_rng(5)
+    a = torch.from_numpy(_packed(rng, 96, 1024)).to(cuda_device)
+    b = torch.from_numpy(_packed(rng, 512, 1024)).to(cuda_device)
+    sx = torch.rand(96, device=cuda_device)
+    sw = torch.rand(512, device=cuda_device)
+    y1 = ops.w4a4_gemm(a, b, sx, sw)
+    y2 = ops.w4a4_gemm(a, b, sx, sw)
+    assert torch.equal(y1, y2)
+
+
+@pytest.mark.parametrize("M,K,N", [(2048, 4096, 4096), (2048, 4096, 11008), (2048, 11008, 4096), (8192, 4096, 4096),
+                                   (1, 4096, 11008), (16, 11008, 4096), (128, 14336, 4096)])
+def test_gemm_full_size_checksums(oracle, cuda_device, M, K, N):
+    """Benchmark sizes: row/column checksums of the int32 accumulators and 512 sampled entries."""
+    from dscquant_b200 import ops
+
+    rng = np.random.default_rng(M + K + N)
+    a = _packed(rng, M, K)
+    b = _packed(rng, N, K)
+    ta, tb = torch.from_numpy(a).to(cuda_device), torch.from_numpy(b).to(cuda_device)
+    sx = torch.ones(M, device=cuda_device)
+    sw = torch.ones(N, device=cuda_device)
+    _, raw = ops.w4a4_gemm(ta, tb, sx, sw, return_raw=True, want_out=False)
+    raw = raw.cpu().numpy().astype(np.int64)
+    A = oracle.unpack_int4(a, K).astype(np.int64)
+    B = oracle.unpack_int4(b, K).astype(np.int64)
+    np.testing.assert_array_equal(raw.sum(1), A @ B.sum(0))
+    np.testing.assert_array_equal(raw.sum(0), B @ A.sum(0))
+    mi = rng.integers(0, M, 512)
+    ni = rng.integers(0, N, 512)
+    np.testing.assert_array_equal(raw[mi, ni], (A[mi] * B[ni]).sum(1))
+
+
+def test_reference_matmul_signature(oracle, cuda_device):
+    """ops.matmul keeps kernel/w4a4.cu:189-225: padded operands, fused / unfused, fp16 / fp32 outputs."""
+    from dscquant_b200 import ops
+
+    rng = np.random.default_rng(9)
+    M, N, KP = 13, 70, 128
+    MP, NP = 16, 72
+    a = _packed(rng, MP, KP)
+    b = _packed(rng, NP, KP)
+    sx = rng.random(MP, dtype=np.float32)
+    sw = rng.random(NP, dtype=np.float32)
+    zx = rng.integers(0, 16, MP).astype(np.int32)
+    sums = oracle.unpack_int4(b, KP).astype(np.int64).sum(1).astype(np.int32)
+    T = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(cuda_device)  # noqa: E731
+    bias = torch.randn(N, device=cuda_device, dtype=torch.float32)
+    out, raw = ops.matmul(T(a), T(b), T(sx), T(zx), T(sw), T(sums), bias, M, N, False, False, True)
+    ref_raw = oracle.gemm_s4(a, b, M, N, KP)
+    np.testing.assert_array_equal(raw.cpu().numpy(), ref_raw)
+    ref = oracle.epilogue(ref_raw, sx[:M], sw[:N], zx[:M], sums[:N], bias.cpu().numpy())
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
+    out16, raw0 = ops.matmul(T(a), T(b), T(sx), T(zx), T(sw), T(sums), bias.half(), M, N, True, True, False)
+    assert raw0.numel() == 0 and out16.dtype == torch.float16
+    np.testing.assert_array_equal(out16.cpu().numpy(), ref.astype(np.float16))
+    with pytest.raises(RuntimeError):
+        ops.matmul(T(a), T(b), T(sx), T(zx), T(sw), T(sums), bias, M, 200, True, False, True)  # b rows < NP
+
+
+def test_no_device_errors_raised(cuda_device):
+    from dscquant_b200 import ops
+
+    assert ops.device_status(cuda_device) == 0

@@ -1,0 +1,138 @@
+"""QuantLinear drop-in on the GPU.
+
+* Reference semantics (reference-style config: asymmetric per-token codes, no rotation) against the
+  reference's own QuantLinear.forward outputs (tests/golden): relative Frobenius error <= 1e-2.
+* Benchmark scheme (QuantConfig(): symmetric codes + online Hadamard rotation) against the oracle's
+  float64 fake-quant restatement: relative Frobenius error <= 1e-2; max-abs error reported."""
+import types
+
+import numpy as np
+import pytest
+import torch
+from torch import nn
+
+from dscquant_b200 import synthetic
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def _f32(bits):
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def _tbf(bits, dev):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def _linear(w_bits, b_bits, dev):
+    N, K = w_bits.shape
+    base = nn.Linear(K, N, bias=b_bits is not None, dtype=torch.bfloat16, device=dev)
+    with torch.no_grad():
+        base.weight.copy_(_tbf(w_bits, dev))
+        if b_bits is not None:
+            base.bias.copy_(_tbf(b_bits, dev))
+    return base
+
+
+@pytest.mark.parametrize("name", ["lin_a", "lin_b", "lin_cfg0"])
+def test_reference_semantics_match_reference_output(golden, cuda_device, name):
+    from dscquant_b200 import QuantLinear
+
+    M, K, N, has_bias = (int(v) for v in golden[f"{name}_shape"])
+    x = golden.get(f"{name}_x", None)
+    w = golden.get(f"{name}_w", None)
+    if x is None:
+        x = synthetic.activations_bf16(M, K, seed=100 + M)
+        w = synthetic.weights_bf16(N, K, seed=200 + N)
+    b = golden[f"{name}_bias"] if has_bias else None
+    ql = QuantLinear(_linear(w, b, cuda_device), types.SimpleNamespace(activation_bits=4, weight_bits=4))
+    ql.enabled = True
+    y = ql(_tbf(x, cuda_device)).float().cpu().numpy()
+    ref = _f32(golden[f"{name}_y"])
+    rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
+    print(f"{name}: rel_fro={rel:.3e} max_abs={np.abs(y - ref).max():.3e}")
+    assert rel <= TOL
+
+
+def _oracle_fake_quant(oracle, x_bits, w_bits, b_bits=None):
+    y = oracle.rotate(_f32(x_bits))
+    wr = oracle.rotate(_f32(w_bits))
+    cx, sx = oracle.activation_codes_sym(y)
+    cw, sw = oracle.weight_codes(wr)
+    out = (cx.astype(np.float64) * sx) @ (cw.astype(np.float64) * sw).T
+    if b_bits is not None:
+        out = out + _f32(b_bits)[None, :]
+    return out
+
+
+@pytest.mark.parametrize("M,K,N", [(16, 4096, 4096), (128, 11008, 512), (64, 14336, 256), (5, 4096, 11008)])
+def test_symmetric_rotated_matches_oracle(oracle, cuda_device, M, K, N):
+    from dscquant_b200 import QuantConfig, QuantLinear
+
+    x = synthetic.activations_bf16(M, K, seed=M)
+    w = synthetic.weights_bf16(N, K, seed=N)
+    ql = QuantLinear(_linear(w, None, cuda_device), QuantConfig())
+    ql.enabled = True
+    y = ql(_tbf(x, cuda_device)).float().cpu().numpy()
+    ref = _oracle_fake_quant(oracle, x, w)
+    rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
+    dense = _f32(x).astype(np.float64) @ _f32(w).astype(np.float64).T
+    rel_dense = np.linalg.norm(y - dense) / np.linalg.norm(dense)
+    print(f"M={M} K={K} N={N}: rel_fro vs fake-quant={rel:.3e} max_abs={np.abs(y - ref).max():.3e} "
+          f"(vs unquantized: {rel_dense:.3e})")
+    assert rel <= TOL
+
+
+def test_rotated_integer_path_exact(oracle, cuda_device):
+    """GPU accumulators of the module equal the oracle's integer GEMM on the module's own packed operands."""
+    from dscquant_b200 import QuantConfig, QuantLinear, ops
+
+    M, K, N = 32, 11008, 384
+    x = synthetic.activations_bf16(M, K, seed=1)
+    w = synthetic.weights_bf16(N, K, seed=2)
+    ql = QuantLinear(_linear(w, None, cuda_device), QuantConfig())
+    ql.enabled = True
+    ql.prepare()
+    q = ops.rowquant(_tbf(x, cuda_device), "act_sym", rotate=True, KP=ql._prep["KP"])
+    out, raw = ops.w4a4_gemm(q.packed, ql._prep["packed"], q.scales, ql._prep["sw"], return_raw=True)
+    a = q.packed.cpu().numpy()
+    b = ql._prep["packed"].cpu().numpy()
+    ref_raw = oracle.gemm_s4(a, b, M, N, ql._prep["KP"])
+    np.testing.assert_array_equal(raw.cpu().numpy(), ref_raw)
+    ref = oracle.epilogue(ref_raw, q.scales.cpu().numpy(), ql._prep["sw"].cpu().numpy())
+    np.testing.assert_array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), oracle.f32_to_bf16_bits(ref))
+    y = ql(_tbf(x, cuda_device))
+    assert torch.equal(y, out)
+
+
+def test_leading_dims_bias_and_prepare_once(cuda_device):
+    from dscquant_b200 import QuantConfig, QuantLinear
+
+    K, N = 4096, 256
+    w = synthetic.weights_bf16(N, K, seed=5)
+    b = synthetic.weights_bf16(1, N, seed=6, std=0.5)[0]
+    ql = QuantLinear(_linear(w, b, cuda_device), QuantConfig())
+    ql.enabled = True
+    x = torch.randn(2, 5, K, device=cuda_device, dtype=torch.bfloat16)
+    y3 = ql(x)
+    packed = ql._prep["packed"]
+    y2 = ql(x.reshape(10, K))
+    assert y3.shape == (2, 5, N) and ql._prep["packed"] is packed
+    assert torch.equal(y3.reshape(10, N), y2)
+    ql.enabled = False
+    torch.testing.assert_close(ql(x), ql.base(x))
+
+
+def test_fp16_and_fp32_inputs(cuda_device):
+    from dscquant_b200 import QuantConfig, QuantLinear
+
+    for dt in (torch.float16, torch.float32):
+        base = nn.Linear(256, 64, dtype=dt, device=cuda_device)
+        ql = QuantLinear(base, QuantConfig())
+        ql.enabled = True
+        x = torch.randn(3, 256, dtype=dt, device=cuda_device)
+        y = ql(x)
+        assert y.dtype == dt
+        rel = (y.float() - base(x).float()).norm() / base(x).float().norm()
+        assert rel < 0.25
