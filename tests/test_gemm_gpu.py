@@ -143,7 +143,8 @@ def test_reference_matmul_signature(oracle, cuda_device):
     np.testing.assert_array_equal(out.cpu().numpy(), ref)
     out16, raw0 = ops.matmul(T(a), T(b), T(sx), T(zx), T(sw), T(sums), bias.half(), M, N, True, True, False)
     assert raw0.numel() == 0 and out16.dtype == torch.float16
-    np.testing.assert_array_equal(out16.cpu().numpy(), ref.astype(np.float16))
+    ref16 = oracle.epilogue(ref_raw, sx[:M], sw[:N], zx[:M], sums[:N], bias.half().float().cpu().numpy())
+    np.testing.assert_array_equal(out16.cpu().numpy(), ref16.astype(np.float16))
     with pytest.raises(RuntimeError):
         ops.matmul(T(a), T(b), T(sx), T(zx), T(sw), T(sums), bias, M, 200, True, False, True)  # b rows < NP
 

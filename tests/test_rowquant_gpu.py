@@ -138,4 +138,4 @@ def test_rotation_preserves_norm_on_gpu_codes(oracle, cuda_device):
     y = oracle.rotate(_f32(x))
     deq = r.codes.cpu().numpy()[:, :4096].astype(np.float32) * r.scales.cpu().numpy()[:, None]
     rel = np.linalg.norm(deq - y) / np.linalg.norm(y)
-    assert rel < 0.15
+    assert rel < 0.2
