@@ -48,7 +48,54 @@ def parse():
     p.add_argument("--replicas", type=int, default=4, help="layer replicas cycled so the working set exceeds L2")
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--kernel-case", choices=["gemm", "quant"], default=None,
+                   help="run REPS launches of one kernel on [M, K] x [N, K] (for profilers) and exit")
+    p.add_argument("--M", type=int, default=8192)
+    p.add_argument("--K", type=int, default=4096)
+    p.add_argument("--N", type=int, default=11008)
+    p.add_argument("--reps", type=int, default=3)
     return p.parse_args()
+
+
+def kernel_case(args) -> None:
+    """A few launches of one kernel on synthetic data, timed with CUDA events (used under ncu)."""
+    import numpy as np
+    import torch
+
+    from dscquant_b200 import ops, synthetic
+
+    dev = torch.device("cuda", 0)
+    bf = lambda b: torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16).to(dev)  # noqa: E731
+    x = bf(synthetic.activations_bf16(args.M, args.K, seed=1))
+    if args.kernel_case == "quant":
+        fn = lambda: ops.rowquant(x, "act_sym", rotate=True, KP=args.K)  # noqa: E731
+        units = args.M * args.K * 2.5 + 4 * args.M
+    else:
+        w = bf(synthetic.weights_bf16(args.N, args.K, seed=2))
+        qw = ops.rowquant(w, "weight_sym", rotate=True, KP=args.K)
+        qx = ops.rowquant(x, "act_sym", rotate=True, KP=args.K)
+        out = torch.empty((args.M, args.N), dtype=torch.bfloat16, device=dev)
+        from dscquant_b200 import _lib
+
+        def fn():
+            _lib.check(_lib.load().dscq_matmul(ops._ptr(qx.packed), ops._ptr(qw.packed), ops._ptr(qx.scales), None,
+                                               ops._ptr(qw.scales), None, None, None, args.M, args.N, args.K,
+                                               _lib.BF16, ops._ptr(out), None, 0, ops._stream(dev)), "matmul")
+        units = 2.0 * args.M * args.N * args.K
+    fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(args.reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    t = min(ts)
+    rate = units / (t * 1e-3) / (1e12 if args.kernel_case == "gemm" else 1e9)
+    print(json.dumps({"kernel_case": args.kernel_case, "M": args.M, "K": args.K, "N": args.N, "ms": t,
+                      "rate": rate, "unit": "TOPS" if args.kernel_case == "gemm" else "GB/s"}))
 
 
 def layer_ops(M: int) -> float:
@@ -176,6 +223,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dist = world > 1 and "RANK" in os.environ
+    if args.kernel_case:
+        kernel_case(args)
+        return
     if args.impl == "reference":
         if dist:
             pass  # other ranks exit without work

@@ -14,6 +14,7 @@
 #include "gemm_w4a4.cuh"
 #include "hadamard.h"
 #include "rowquant.cuh"
+#include "wht_quant.cuh"
 
 namespace {
 
@@ -129,6 +130,17 @@ int launch_gemm_kernel(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dsc
   return DSCQ_OK;
 }
 
+template <int LOGK>
+cudaError_t launch_wht(const dscq::RowQuantParams& p, cudaStream_t st) {
+  using C = dscq::WhtCfg<LOGK>;
+  cudaError_t e = cudaFuncSetAttribute(dscq::wht_quant_pow2<LOGK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM);
+  if (e != cudaSuccess) return e;
+  const unsigned grid = static_cast<unsigned>((p.rows_out + C::ROWS - 1) / C::ROWS);
+  dscq::wht_quant_pow2<LOGK><<<grid, C::THREADS, C::SMEM, st>>>(p);
+  return cudaGetLastError();
+}
+
 template <int BN, bool SWAP>
 int dispatch_split(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq::GemmParams& gp,
                    cudaStream_t stream) {
@@ -229,6 +241,22 @@ int dscq_rowquant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x
   p.codes = codes;
   p.ld_codes = ld_codes;
 
+  cudaStream_t cst = static_cast<cudaStream_t>(stream);
+  const bool fast = rotate && p.rot_a == 1 && log2b >= 10 && log2b <= 13 &&
+                    (mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM) && x_dtype == DSCQ_BF16 && KP == K &&
+                    aligned(x, 16) && ld_x % 8 == 0 && aligned(packed, 2) && ld_packed % 2 == 0;
+  if (fast) {
+    cudaError_t e = cudaSuccess;
+    switch (log2b) {
+      case 10: e = launch_wht<10>(p, cst); break;
+      case 11: e = launch_wht<11>(p, cst); break;
+      case 12: e = launch_wht<12>(p, cst); break;
+      default: e = launch_wht<13>(p, cst); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "launch wht_quant_pow2");
+    return DSCQ_OK;
+  }
+
   constexpr int T = 512;
   size_t smem = static_cast<size_t>(K) * sizeof(float) * ((rotate && p.rot_a > 32) ? 2 : 1);
   if (smem > 220 * 1024)
@@ -236,7 +264,7 @@ int dscq_rowquant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x
   cudaError_t e = cudaFuncSetAttribute(dscq::rowquant_smem<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowquant)");
-  dscq::rowquant_smem<T><<<static_cast<unsigned>(rows_out), T, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  dscq::rowquant_smem<T><<<static_cast<unsigned>(rows_out), T, smem, cst>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch rowquant");
   return DSCQ_OK;
