@@ -15,6 +15,7 @@
 #include "hadamard.h"
 #include "rowquant.cuh"
 #include "wht_quant.cuh"
+#include "kron_quant.cuh"
 
 namespace {
 
@@ -141,6 +142,16 @@ cudaError_t launch_wht(const dscq::RowQuantParams& p, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+template <int AP>
+cudaError_t launch_kron(const dscq::RowQuantParams& p, int a, int s, cudaStream_t st) {
+  using C = dscq::KronCfg<AP>;
+  cudaError_t e = cudaFuncSetAttribute(dscq::kron_quant<AP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const int grid = std::min(p.rows_out, num_sms());
+  dscq::kron_quant<AP><<<grid, C::THREADS, C::SMEM, st>>>(p, a, s);
+  return cudaGetLastError();
+}
+
 template <int BN, bool SWAP>
 int dispatch_split(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq::GemmParams& gp,
                    cudaStream_t stream) {
@@ -254,6 +265,17 @@ int dscq_rowquant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x
       default: e = launch_wht<13>(p, cst); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "launch wht_quant_pow2");
+    return DSCQ_OK;
+  }
+
+  // Kronecker path: K = a' * 64 with the dense factor H' = H_a (x) H_(2^s), a' <= 224
+  const int s_log = log2b - 6;
+  const int ap = p.rot_a << (s_log > 0 ? s_log : 0);
+  const bool kron = rotate && p.rot_a > 1 && s_log >= 0 && ap <= 224 && (mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM) &&
+                    x_dtype == DSCQ_BF16 && KP == K && aligned(x, 16) && ld_x % 8 == 0;
+  if (kron) {
+    cudaError_t e = ap <= 176 ? launch_kron<176>(p, p.rot_a, s_log, cst) : launch_kron<224>(p, p.rot_a, s_log, cst);
+    if (e != cudaSuccess) return cuda_fail(e, "launch kron_quant");
     return DSCQ_OK;
   }
 
