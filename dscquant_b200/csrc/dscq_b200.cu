@@ -152,6 +152,21 @@ cudaError_t launch_kron(const dscq::RowQuantParams& p, int a, int s, cudaStream_
   return cudaGetLastError();
 }
 
+template <int BN>
+int launch_gemm_persistent(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq::GemmParams& gp,
+                           cudaStream_t stream) {
+  using C = dscq::PCfg<BN>;
+  auto kern = dscq::w4a4_gemm_persistent<BN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a4_gemm_persistent)");
+  const int tiles = gp.tiles_i * gp.tiles_j;
+  const int grid = std::min(tiles, num_sms());
+  kern<<<grid, dscq::kGemmThreads, C::kSmemBytes, stream>>>(tmP, tmQ, gp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_persistent");
+  return DSCQ_OK;
+}
+
 template <int BN, bool SWAP>
 int dispatch_split(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq::GemmParams& gp,
                    cudaStream_t stream) {
@@ -317,25 +332,36 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   int st = check_device(nullptr);
   if (st) return st;
 
+  if (KP > 65536)
+    return fail(DSCQ_ERR_UNSUPPORTED, "KP > 65536: the int8 tensor-core accumulation (256 * sum) would overflow int32");
   const int64_t kbytes = KP / 2;
   const int kblocks = static_cast<int>((KP + 127) / 128);
   const bool swap = variant == DSCQ_GEMM_SMALL_M || (variant == DSCQ_GEMM_AUTO && M <= 64);
+  const int nsm = num_sms();
   int BN;
   int64_t ti, tj;
+  int splits = 1;
+  bool persistent = false;
   if (swap) {
     BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     ti = (N + 127) / 128;
     tj = (M + BN - 1) / BN;
+    while (splits < 8 && ti * tj * splits * 2 <= nsm && kblocks >= splits * 2 * 2) splits *= 2;
   } else {
-    const int64_t t256 = ((M + 127) / 128) * ((N + 255) / 256);
-    BN = t256 >= num_sms() ? 256 : 128;
     ti = (M + 127) / 128;
+    const int64_t t256 = ti * ((N + 255) / 256), t128 = ti * ((N + 127) / 128);
+    auto eff = [&](int64_t t) { return static_cast<double>(t) / (((t + nsm - 1) / nsm) * nsm); };
+    if (t128 * 2 <= nsm) {
+      BN = 128;  // too few tiles: split K across a cluster
+      while (splits < 8 && t128 * splits * 2 <= nsm && kblocks >= splits * 2 * 2) splits *= 2;
+    } else {
+      BN = (t256 >= nsm / 2 && eff(t256) + 0.1 >= eff(t128)) ? 256 : 128;
+    }
     tj = (N + BN - 1) / BN;
+    persistent = splits == 1;
   }
   const int64_t tiles = ti * tj;
   DSCQ_REQUIRE(tiles * 8 < (int64_t(1) << 31), "problem too large");
-  int splits = 1;
-  while (splits < 8 && tiles * splits * 2 <= num_sms() && kblocks >= splits * 2 * 2) splits *= 2;
 
   CUtensorMap tmP, tmQ;
   const uint8_t* P = swap ? b : a;
@@ -365,6 +391,7 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   gp.vec_out = (out && aligned(out, 16) && (N % 8 == 0)) ? 1 : 0;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (persistent) return BN == 256 ? launch_gemm_persistent<256>(tmP, tmQ, gp, s) : launch_gemm_persistent<128>(tmP, tmQ, gp, s);
   if (swap) {
     if (BN == 16) return dispatch_split<16, true>(tmP, tmQ, gp, s);
     if (BN == 32) return dispatch_split<32, true>(tmP, tmQ, gp, s);

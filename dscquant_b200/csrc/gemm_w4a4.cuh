@@ -1,5 +1,5 @@
 // W4A4 GEMM for sm_100a: packed-int4 operands -> TMA -> shared memory ->
-// sign-extension to int8 in the UMMA canonical 128B-swizzled layout ->
+// int8 expansion in the UMMA canonical 128B-swizzled layout ->
 // tcgen05.mma.kind::i8 with int32 accumulators in TMEM -> fused dequant
 // epilogue (token scale x channel scale, optional zero-point term, bias,
 // residual) -> bf16/f16/f32.
@@ -10,15 +10,30 @@
 // kernel/w4a4.cu:70-78. Rounding is explicit (no FMA contraction) so the
 // epilogue is reproducible bit-for-bit from the same int32 accumulators.
 //
-// Tile roles (448 threads, one CTA per SM):
+// int4 -> int8 expansion: each nibble goes to the HIGH half of its byte
+// (byte = nibble << 4), i.e. the int8 value 16*code. Both operands are
+// expanded this way, so the tensor cores accumulate 256 * sum(a*b) exactly
+// (|256 * 64 * KP| < 2^31 for KP <= 65536) and the epilogue shifts right by 8.
+// One 32-bit word of 8 nibbles becomes two words with 3 integer ops:
+// (w << 4) & 0xF0F0F0F0 (nibbles 0,2,4,6) and w & 0xF0F0F0F0 (1,3,5,7); the
+// same permutation inside every 8-element group is applied to both operands,
+// so it cancels in the dot product.
+//
+// Kernels
+//   w4a4_gemm_tc<BN, SWAP, SPLIT>  one output tile per CTA; SWAP puts the
+//       weights on the 128-row MMA side (small M: tokens become the MMA N
+//       dimension, 16..64); SPLIT splits K across the CTAs of a cluster and
+//       sums the partial int32 tiles through distributed shared memory.
+//   w4a4_gemm_persistent<BN>  large M: persistent CTAs walk the tile list;
+//       two TMEM accumulators so the epilogue of one tile overlaps the
+//       main loop of the next; raw (TMA) and expanded stages are counted
+//       separately (more raw stages in flight to cover load latency).
+//
+// Warp roles (448 threads, one CTA per SM):
 //   warps 0-3   epilogue   (warp w owns TMEM lanes 32w..32w+31 = tile rows)
 //   warp  4     TMA producer (one lane)
 //   warp  5     TMEM allocator + MMA issuer (one lane)
 //   warps 6-13  int4 -> int8 expansion (256 threads)
-// The MMA "P" operand (128 rows, TMEM lanes) is the activation tile, or the
-// weight tile when SWAP is set (small M: tokens become the MMA N dimension).
-// SPLIT splits the K loop across the CTAs of a thread-block cluster; partial
-// int32 tiles are summed through distributed shared memory by cluster rank 0.
 #pragma once
 #include "ptx.cuh"
 
@@ -43,25 +58,9 @@ struct GemmParams {
   int vec_out;           // 1: out rows allow 16-byte vector stores of 16-column groups
 };
 
-template <int BN>
-struct GemmCfg {
-  static constexpr int kThreads = 448;
-  static constexpr int kExpandWarps = 8;
-  static constexpr int kExpandThreads = kExpandWarps * 32;
-  static constexpr int kRows = 128 + BN;           // P rows + Q rows per stage
-  static constexpr int kRawStage = kRows * 64;      // packed int4 bytes per stage
-  static constexpr int kExpP = 128 * 128;           // expanded int8 bytes, P
-  static constexpr int kExpStage = kRows * 128;     // expanded int8 bytes per stage
-  static constexpr int kStages = (216 * 1024) / (kRawStage + kExpStage);
-  static constexpr int kRedStride = BN + 4;         // int32 words per row of the split-K exchange tile
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  static constexpr int kBarBytes = (4 * kStages + 1) * 8 + 16;
-  static constexpr int kSmemBytes = 1024 + kStages * (kRawStage + kExpStage) + kBarBytes;
-  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16,256]");
-  static_assert(kStages >= 2, "pipeline needs two stages");
-  static_assert(128 * kRedStride * 4 <= kStages * kExpStage, "split-K exchange tile must fit in the stage buffers");
-  static_assert((kExpStage % 1024) == 0, "swizzle atoms must stay 1024-byte aligned");
-};
+constexpr int kGemmThreads = 448;
+constexpr int kExpandWarps = 8;
+constexpr int kExpandThreads = kExpandWarps * 32;
 
 __device__ __forceinline__ float epi_scale(int32_t acc, float s_row, float s_col) {
   return __fmul_rn(__fmul_rn(__int2float_rn(acc), s_row), s_col);
@@ -82,8 +81,108 @@ __device__ __forceinline__ void store_from_float(void* p, int64_t idx, int dtype
     reinterpret_cast<float*>(p)[idx] = v;
 }
 
+// Expands one 16-byte chunk (32 nibbles) of row r into 32 bytes at logical
+// K-byte offset 32c of that row in a 128B-swizzled operand tile.
+__device__ __forceinline__ void expand_chunk(const uint4 w, uint8_t* tile, int r, int c) {
+  constexpr uint32_t M = 0xF0F0F0F0u;
+  const uint4 o0 = make_uint4((w.x << 4) & M, w.x & M, (w.y << 4) & M, w.y & M);
+  const uint4 o1 = make_uint4((w.z << 4) & M, w.z & M, (w.w << 4) & M, w.w & M);
+  uint8_t* rowp = tile + r * 128;
+  const int sw = r & 7;
+  *reinterpret_cast<uint4*>(rowp + (((2 * c) ^ sw) << 4)) = o0;
+  *reinterpret_cast<uint4*>(rowp + (((2 * c + 1) ^ sw) << 4)) = o1;
+}
+
+// Epilogue for 16 consecutive accumulator columns j0..j0+15 of tile row
+// `row_local`; acc[] are the true sums (already divided by 256).
+template <int BN, bool SWAP>
+__device__ __forceinline__ void epilogue16(const GemmParams& p, int ti, int tj, int row_local, int j0,
+                                           const int32_t (&acc)[16]) {
+  const bool has_bias = p.bias != nullptr, has_res = p.residual != nullptr;
+  const bool asym = p.zx != nullptr;
+  if constexpr (!SWAP) {
+    const int m = ti * 128 + row_local;
+    const int n0 = tj * BN + j0;
+    if (m >= p.M) return;
+    const float sxm = p.sx[m];
+    const int32_t zc = asym ? 8 - p.zx[m] : 0;
+    const int64_t o0 = static_cast<int64_t>(m) * p.N + n0;
+    const bool full = n0 + 16 <= p.N;
+    if (p.raw) {
+#pragma unroll
+      for (int t = 0; t < 16; ++t)
+        if (n0 + t < p.N) p.raw[o0 + t] = acc[t];
+    }
+    if (p.out) {
+      float f[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const int n = full ? n0 + t : min(n0 + t, p.N - 1);
+        f[t] = epi_scale(asym ? acc[t] + zc * p.wsum[n] : acc[t], sxm, p.sw[n]);
+        if (has_bias) f[t] = __fadd_rn(f[t], load_as_float(p.bias, n, p.out_dtype));
+        if (has_res) f[t] = __fadd_rn(f[t], load_as_float(p.residual, o0 + (n - n0), p.out_dtype));
+      }
+      if (full && p.vec_out && p.out_dtype == kOutBF16) {
+        uint32_t w[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * t], f[2 * t + 1]);
+          w[t] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + o0);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 16; ++t)
+          if (n0 + t < p.N) store_from_float(p.out, o0 + t, p.out_dtype, f[t]);
+      }
+    }
+  } else {
+    const int n = ti * 128 + row_local;
+    if (n >= p.N) return;
+    const float swn = p.sw[n];
+    const int32_t wsn = asym ? p.wsum[n] : 0;
+    const float bn = has_bias ? load_as_float(p.bias, n, p.out_dtype) : 0.f;
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const int m = tj * BN + j0 + t;
+      if (m < p.M) {
+        const int64_t o = static_cast<int64_t>(m) * p.N + n;
+        if (p.raw) p.raw[o] = acc[t];
+        if (p.out) {
+          const int32_t corr = asym ? acc[t] + (8 - p.zx[m]) * wsn : acc[t];
+          float f = epi_scale(corr, p.sx[m], swn);
+          if (has_bias) f = __fadd_rn(f, bn);
+          if (has_res) f = __fadd_rn(f, load_as_float(p.residual, o, p.out_dtype));
+          store_from_float(p.out, o, p.out_dtype, f);
+        }
+      }
+    }
+  }
+}
+
+// ============================================================ one tile per CTA (small M, split K)
+template <int BN>
+struct GemmCfg {
+  static constexpr int kThreads = kGemmThreads;
+  static constexpr int kRows = 128 + BN;           // P rows + Q rows per stage
+  static constexpr int kRawStage = kRows * 64;      // packed int4 bytes per stage
+  static constexpr int kExpP = 128 * 128;           // expanded int8 bytes, P
+  static constexpr int kExpStage = kRows * 128;     // expanded int8 bytes per stage
+  static constexpr int kStages = (216 * 1024) / (kRawStage + kExpStage);
+  static constexpr int kRedStride = BN + 4;         // int32 words per row of the split-K exchange tile
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr int kBarBytes = (4 * kStages + 1) * 8 + 16;
+  static constexpr int kSmemBytes = 1024 + kStages * (kRawStage + kExpStage) + kBarBytes;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16,256]");
+  static_assert(kStages >= 2, "pipeline needs two stages");
+  static_assert(128 * kRedStride * 4 <= kStages * kExpStage, "split-K exchange tile must fit in the stage buffers");
+  static_assert((kExpStage % 1024) == 0, "swizzle atoms must stay 1024-byte aligned");
+};
+
 template <int BN, bool SWAP, bool SPLIT>
-__global__ void __launch_bounds__(448, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     w4a4_gemm_tc(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                  const GemmParams p) {
   using C = GemmCfg<BN>;
@@ -112,8 +211,8 @@ __global__ void __launch_bounds__(448, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], C::kExpandWarps);
-      mbar_init(&exp_full[s], C::kExpandWarps);
+      mbar_init(&raw_empty[s], kExpandWarps);
+      mbar_init(&exp_full[s], kExpandWarps);
       mbar_init(&exp_empty[s], 1);
     }
     mbar_init(tmem_full, 1);
@@ -183,19 +282,13 @@ __global__ void __launch_bounds__(448, 1)
       if (i >= S && !mbar_wait(&exp_empty[s], ph ^ 1u, abort_flag)) break;
       const uint8_t* src = raw_base + s * C::kRawStage;
       uint8_t* dstP = exp_base + s * C::kExpStage;
-      for (int u = et; u < C::kRows * 4; u += C::kExpandThreads) {
-        const int row = u >> 2, c = u & 3;
+      for (int u = et; u < C::kRows * 4; u += kExpandThreads) {
+        const int row = u >> 2;
         const uint4 w = *reinterpret_cast<const uint4*>(src + u * 16);
-        uint4 o0, o1;
-        s4x8_to_s8x8(w.x, o0.x, o0.y);
-        s4x8_to_s8x8(w.y, o0.z, o0.w);
-        s4x8_to_s8x8(w.z, o1.x, o1.y);
-        s4x8_to_s8x8(w.w, o1.z, o1.w);
-        const int r = row < 128 ? row : row - 128;
-        uint8_t* rowp = (row < 128 ? dstP : dstP + C::kExpP) + r * 128;
-        const int sw = r & 7;
-        *reinterpret_cast<uint4*>(rowp + (((2 * c) ^ sw) << 4)) = o0;
-        *reinterpret_cast<uint4*>(rowp + (((2 * c + 1) ^ sw) << 4)) = o1;
+        if (row < 128)
+          expand_chunk(w, dstP, row, u & 3);
+        else
+          expand_chunk(w, dstP + C::kExpP, row - 128, u & 3);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -223,23 +316,21 @@ __global__ void __launch_bounds__(448, 1)
         int4* dst = reinterpret_cast<int4*>(red + row_local * C::kRedStride + j0);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-          dst[q] = make_int4(static_cast<int>(r[4 * q]), static_cast<int>(r[4 * q + 1]),
-                             static_cast<int>(r[4 * q + 2]), static_cast<int>(r[4 * q + 3]));
+          dst[q] = make_int4(static_cast<int>(r[4 * q]) >> 8, static_cast<int>(r[4 * q + 1]) >> 8,
+                             static_cast<int>(r[4 * q + 2]) >> 8, static_cast<int>(r[4 * q + 3]) >> 8);
       }
     }
   }
   __syncwarp();
   if constexpr (SPLIT) cluster_sync();
   if (warp < 4 && (!SPLIT || z == 0) && tile_ok) {
-    const bool has_bias = p.bias != nullptr, has_res = p.residual != nullptr;
-    const bool asym = p.zx != nullptr;
     for (int j0 = 0; j0 < BN; j0 += 16) {
       uint32_t r[16];
       tmem_ld16(t_row + j0, r);
       tmem_ld_wait();
       int32_t acc[16];
 #pragma unroll
-      for (int t = 0; t < 16; ++t) acc[t] = static_cast<int32_t>(r[t]);
+      for (int t = 0; t < 16; ++t) acc[t] = static_cast<int32_t>(r[t]) >> 8;
       if constexpr (SPLIT) {
         const uint32_t local = smem_u32(red + row_local * C::kRedStride + j0);
         for (int q = 1; q < p.splits; ++q) {
@@ -254,68 +345,7 @@ __global__ void __launch_bounds__(448, 1)
           }
         }
       }
-      if constexpr (!SWAP) {
-        const int m = ti * 128 + row_local;
-        const int n0 = tj * BN + j0;
-        if (m < p.M) {
-          const float sxm = p.sx[m];
-          const int32_t zc = asym ? 8 - p.zx[m] : 0;
-          const int64_t o0 = static_cast<int64_t>(m) * p.N + n0;
-          const bool full = n0 + 16 <= p.N;
-          if (p.raw) {
-#pragma unroll
-            for (int t = 0; t < 16; ++t)
-              if (n0 + t < p.N) p.raw[o0 + t] = acc[t];
-          }
-          if (p.out) {
-            float f[16];
-#pragma unroll
-            for (int t = 0; t < 16; ++t) {
-              const int n = full ? n0 + t : min(n0 + t, p.N - 1);
-              f[t] = epi_scale(asym ? acc[t] + zc * p.wsum[n] : acc[t], sxm, p.sw[n]);
-              if (has_bias) f[t] = __fadd_rn(f[t], load_as_float(p.bias, n, p.out_dtype));
-              if (has_res) f[t] = __fadd_rn(f[t], load_as_float(p.residual, o0 + (n - n0), p.out_dtype));
-            }
-            if (full && p.vec_out && p.out_dtype == kOutBF16) {
-              uint32_t w[8];
-#pragma unroll
-              for (int t = 0; t < 8; ++t) {
-                __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * t], f[2 * t + 1]);
-                w[t] = *reinterpret_cast<uint32_t*>(&h2);
-              }
-              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + o0);
-              dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-              dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-            } else {
-#pragma unroll
-              for (int t = 0; t < 16; ++t)
-                if (n0 + t < p.N) store_from_float(p.out, o0 + t, p.out_dtype, f[t]);
-            }
-          }
-        }
-      } else {
-        const int n = ti * 128 + row_local;
-        if (n < p.N) {
-          const float swn = p.sw[n];
-          const int32_t wsn = asym ? p.wsum[n] : 0;
-          const float bn = has_bias ? load_as_float(p.bias, n, p.out_dtype) : 0.f;
-#pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            const int m = tj * BN + j0 + t;
-            if (m < p.M) {
-              const int64_t o = static_cast<int64_t>(m) * p.N + n;
-              if (p.raw) p.raw[o] = acc[t];
-              if (p.out) {
-                const int32_t corr = asym ? acc[t] + (8 - p.zx[m]) * wsn : acc[t];
-                float f = epi_scale(corr, p.sx[m], swn);
-                if (has_bias) f = __fadd_rn(f, bn);
-                if (has_res) f = __fadd_rn(f, load_as_float(p.residual, o, p.out_dtype));
-                store_from_float(p.out, o, p.out_dtype, f);
-              }
-            }
-          }
-        }
-      }
+      epilogue16<BN, SWAP>(p, ti, tj, row_local, j0, acc);
     }
   }
   __syncwarp();
@@ -329,6 +359,205 @@ __global__ void __launch_bounds__(448, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_d, C::kTmemCols);
+  }
+}
+
+// ============================================================ persistent (large M)
+template <int BN>
+struct PCfg {
+  static constexpr int kRows = 128 + BN;
+  static constexpr int kRawStage = kRows * 64;
+  static constexpr int kExpP = 128 * 128;
+  static constexpr int kExpStage = kRows * 128;
+  static constexpr int ES = BN >= 256 ? 2 : 3;                                   // expanded stages
+  static constexpr int RS = (216 * 1024 - ES * kExpStage) / kRawStage;           // raw (TMA) stages
+  static constexpr int UPT = kRows * 4 / kExpandThreads;                         // 16-B chunks per thread
+  static constexpr int kTmemCols = 2 * BN;                                       // two accumulators
+  static constexpr int kBarBytes = (2 * RS + 2 * ES + 5) * 8 + 16;
+  static constexpr int kSmemBytes = 1024 + ES * kExpStage + RS * kRawStage + kBarBytes;
+  static_assert(BN == 128 || BN == 256, "persistent kernel uses N tiles of 128 or 256");
+  static_assert(RS >= 2, "need two raw stages");
+  static_assert(kRows * 4 % kExpandThreads == 0, "expansion chunks must divide evenly");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    w4a4_gemm_persistent(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
+                         const GemmParams p) {
+  using C = PCfg<BN>;
+  constexpr int RS = C::RS, ES = C::ES;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* exp_base = smem;
+  uint8_t* raw_base = smem + ES * C::kExpStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw_base + RS * C::kRawStage);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = bars + RS;
+  uint64_t* exp_full = bars + 2 * RS;
+  uint64_t* exp_empty = bars + 2 * RS + ES;
+  uint64_t* tmem_full = bars + 2 * RS + 2 * ES;   // [2]
+  uint64_t* tmem_empty = tmem_full + 2;           // [2]
+  uint64_t* mma_done = tmem_full + 4;             // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = p.tiles_i * p.tiles_j;
+  const int kb_n = p.kblocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], kExpandWarps);
+    }
+    for (int s = 0; s < ES; ++s) {
+      mbar_init(&exp_full[s], kExpandWarps);
+      mbar_init(&exp_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmP);
+    tma_prefetch_desc(&tmQ);
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+        const int ti = tile % p.tiles_i, tj = tile / p.tiles_i;
+        for (int kb = 0; kb < kb_n; ++kb, ++g) {
+          const int s = g % RS;
+          if (g >= RS && !mbar_wait(&raw_empty[s], ((g / RS) & 1u) ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&raw_full[s], C::kRawStage);
+          uint8_t* dst = raw_base + s * C::kRawStage;
+          tma_load_2d(dst, &tmP, &raw_full[s], kb * 64, ti * 128);
+          tma_load_2d(dst + 128 * 64, &tmQ, &raw_full[s], kb * 64, tj * BN);
+        }
+      }
+      if (!ok) {
+        for (int j = g > RS ? g - RS : 0; j < g; ++j) mbar_wait(&raw_full[j % RS], (j / RS) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_i8(128, BN);
+      int g = 0, t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++t) {
+        const int acc = t & 1, use = t >> 1;
+        if (use > 0 && !mbar_wait(&tmem_empty[acc], (use - 1) & 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kb_n; ++kb, ++g) {
+          const int s = g % ES;
+          if (!mbar_wait(&exp_full[s], (g / ES) & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t aP = smem_u32(exp_base + s * C::kExpStage);
+          const uint64_t da = umma_desc_sw128(aP);
+          const uint64_t db = umma_desc_sw128(aP + C::kExpP);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_i8_ss(d, da + 2 * kk, db + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&exp_empty[s]);
+        }
+        if (ok) umma_commit(&tmem_full[acc]);
+      }
+      umma_commit(mma_done);
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------ int4 -> int8 expansion
+    const int et = threadIdx.x - 6 * 32;
+    int g = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+      for (int kb = 0; kb < kb_n; ++kb, ++g) {
+        const int rs = g % RS, es = g % ES;
+        if (!mbar_wait(&raw_full[rs], (g / RS) & 1u, abort_flag) ||
+            (g >= ES && !mbar_wait(&exp_empty[es], ((g / ES) & 1u) ^ 1u, abort_flag))) {
+          ok = false;
+          break;
+        }
+        const uint8_t* src = raw_base + rs * C::kRawStage;
+        uint8_t* dstP = exp_base + es * C::kExpStage;
+        uint4 w[C::UPT];
+#pragma unroll
+        for (int i = 0; i < C::UPT; ++i) w[i] = *reinterpret_cast<const uint4*>(src + (et + i * kExpandThreads) * 16);
+#pragma unroll
+        for (int i = 0; i < C::UPT; ++i) {
+          const int u = et + i * kExpandThreads;
+          const int row = u >> 2;
+          if (i * kExpandThreads < 128 * 4)  // compile-time: chunk block i lies in P or in Q
+            expand_chunk(w[i], dstP, row, u & 3);
+          else
+            expand_chunk(w[i], dstP + C::kExpP, row - 128, u & 3);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&raw_empty[rs]);
+          mbar_arrive(&exp_full[es]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 0-3)
+    const int row_local = warp * 32 + lane;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t) {
+      const int acc_i = t & 1, use = t >> 1;
+      bool ok = mbar_wait(&tmem_full[acc_i], use & 1u, abort_flag);
+      ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      const int ti = tile % p.tiles_i, tj = tile / p.tiles_i;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(acc_i * BN);
+      for (int j0 = 0; j0 < BN; j0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_row + j0, r);
+        tmem_ld_wait();
+        int32_t acc[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) acc[q] = static_cast<int32_t>(r[q]) >> 8;
+        epilogue16<BN, false>(p, ti, tj, row_local, j0, acc);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[acc_i]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    if (lane == 0) mbar_wait(mma_done, 0, nullptr);  // every issued MMA has retired
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
   }
 }
 
