@@ -54,6 +54,7 @@ def parse():
     p.add_argument("--K", type=int, default=4096)
     p.add_argument("--N", type=int, default=11008)
     p.add_argument("--reps", type=int, default=3)
+    p.add_argument("--variant", type=int, default=0, help="dscq_matmul variant for --kernel-case gemm")
     return p.parse_args()
 
 
@@ -80,7 +81,8 @@ def kernel_case(args) -> None:
         def fn():
             _lib.check(_lib.load().dscq_matmul(ops._ptr(qx.packed), ops._ptr(qw.packed), ops._ptr(qx.scales), None,
                                                ops._ptr(qw.scales), None, None, None, args.M, args.N, args.K,
-                                               _lib.BF16, ops._ptr(out), None, 0, ops._stream(dev)), "matmul")
+                                               _lib.BF16, ops._ptr(out), None, args.variant, ops._stream(dev)),
+                        "matmul")
         units = 2.0 * args.M * args.N * args.K
     fn()
     torch.cuda.synchronize()
@@ -94,7 +96,7 @@ def kernel_case(args) -> None:
         ts.append(e0.elapsed_time(e1))
     t = min(ts)
     rate = units / (t * 1e-3) / (1e12 if args.kernel_case == "gemm" else 1e9)
-    print(json.dumps({"kernel_case": args.kernel_case, "M": args.M, "K": args.K, "N": args.N, "ms": t,
+    print(json.dumps({"kernel_case": args.kernel_case, "variant": args.variant, "M": args.M, "K": args.K, "N": args.N, "ms": t,
                       "rate": rate, "unit": "TOPS" if args.kernel_case == "gemm" else "GB/s"}))
 
 

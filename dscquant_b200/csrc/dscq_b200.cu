@@ -137,7 +137,8 @@ cudaError_t launch_wht(const dscq::RowQuantParams& p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(dscq::wht_quant_pow2<LOGK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM);
   if (e != cudaSuccess) return e;
-  const unsigned grid = static_cast<unsigned>((p.rows_out + C::ROWS - 1) / C::ROWS);
+  const int batches = (p.rows_out + C::ROWS - 1) / C::ROWS;
+  const unsigned grid = static_cast<unsigned>(std::min(batches, 2 * num_sms()));
   dscq::wht_quant_pow2<LOGK><<<grid, C::THREADS, C::SMEM, st>>>(p);
   return cudaGetLastError();
 }
@@ -164,6 +165,20 @@ int launch_gemm_persistent(const CUtensorMap& tmP, const CUtensorMap& tmQ, const
   kern<<<grid, dscq::kGemmThreads, C::kSmemBytes, stream>>>(tmP, tmQ, gp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_persistent");
+  return DSCQ_OK;
+}
+
+template <int BN>
+int launch_gemm_ldg(const dscq::GemmParams& gp, cudaStream_t stream) {
+  using C = dscq::LCfg<BN>;
+  auto kern = dscq::w4a4_gemm_persistent_ldg<BN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a4_gemm_persistent_ldg)");
+  const int tiles = gp.tiles_i * gp.tiles_j;
+  const int grid = std::min(tiles, num_sms());
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(gp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_persistent_ldg");
   return DSCQ_OK;
 }
 
@@ -328,7 +343,7 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   DSCQ_REQUIRE(!zx || sums, "asymmetric activations (zx) need weight code sums");
   DSCQ_REQUIRE(out_dtype == DSCQ_BF16 || out_dtype == DSCQ_F16 || out_dtype == DSCQ_F32, "out_dtype must be bf16/f16/f32");
   DSCQ_REQUIRE(aligned(a, 16) && aligned(b, 16), "packed operands must be 16-byte aligned");
-  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_LARGE_M, "unknown GEMM variant");
+  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_LARGE_M_TMA, "unknown GEMM variant");
   int st = check_device(nullptr);
   if (st) return st;
 
@@ -389,9 +404,16 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   gp.raw = raw;
   gp.out_dtype = out_dtype;
   gp.vec_out = (out && aligned(out, 16) && (N % 8 == 0)) ? 1 : 0;
+  gp.P = P;
+  gp.Q = Q;
+  gp.kbytes = static_cast<int>(kbytes);
+  gp.rowsP = static_cast<int>(rowsP);
+  gp.rowsQ = static_cast<int>(rowsQ);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (persistent) return BN == 256 ? launch_gemm_persistent<256>(tmP, tmQ, gp, s) : launch_gemm_persistent<128>(tmP, tmQ, gp, s);
+  if (persistent && variant == DSCQ_GEMM_LARGE_M_TMA)
+    return BN == 256 ? launch_gemm_persistent<256>(tmP, tmQ, gp, s) : launch_gemm_persistent<128>(tmP, tmQ, gp, s);
+  if (persistent) return BN == 256 ? launch_gemm_ldg<256>(gp, s) : launch_gemm_ldg<128>(gp, s);
   if (swap) {
     if (BN == 16) return dispatch_split<16, true>(tmP, tmQ, gp, s);
     if (BN == 32) return dispatch_split<32, true>(tmP, tmQ, gp, s);

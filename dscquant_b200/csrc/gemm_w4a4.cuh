@@ -56,6 +56,11 @@ struct GemmParams {
   int32_t* raw;          // [M, N] int32 accumulators, or null
   int out_dtype;
   int vec_out;           // 1: out rows allow 16-byte vector stores of 16-column groups
+  // direct-load kernels: operand base pointers, packed row length and row counts
+  const uint8_t* P;
+  const uint8_t* Q;
+  int kbytes;
+  int rowsP, rowsQ;
 };
 
 constexpr int kGemmThreads = 448;
@@ -555,6 +560,205 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == 5) {
     if (lane == 0) mbar_wait(mma_done, 0, nullptr);  // every issued MMA has retired
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ============================================================ persistent, direct loads
+// Same tile loop, TMEM double buffering and epilogue as w4a4_gemm_persistent,
+// but the expansion warps read the packed int4 bytes straight from L2 with
+// 16-byte non-allocating loads, three K blocks ahead in registers, instead of
+// staging them through shared memory with TMA. Shared memory then only holds
+// the expanded int8 stages (written once by the expansion warps, read once by
+// the tensor cores): half the shared-memory traffic per K block.
+//   warps 0-3 epilogue, warp 4 TMEM allocator + MMA issuer, warps 5-12 expansion.
+template <int BN>
+struct LCfg {
+  static constexpr int kThreads = 416;
+  static constexpr int kRows = 128 + BN;
+  static constexpr int kExpP = 128 * 128;
+  static constexpr int kExpStage = kRows * 128;
+  static constexpr int ES = (192 * 1024) / kExpStage;
+  static constexpr int UPT = kRows * 4 / kExpandThreads;
+  static constexpr int D = 3;                      // K blocks in flight per expansion thread
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kBarBytes = (2 * ES + 5) * 8 + 16;
+  static constexpr int kSmemBytes = 1024 + ES * kExpStage + kBarBytes;
+  static_assert(BN == 128 || BN == 256, "direct-load kernel uses N tiles of 128 or 256");
+  static_assert(ES >= 2, "need two expanded stages");
+  static_assert(kRows * 4 % kExpandThreads == 0, "expansion chunks must divide evenly");
+};
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(416, 1) w4a4_gemm_persistent_ldg(const GemmParams p) {
+  using C = LCfg<BN>;
+  constexpr int ES = C::ES, UPT = C::UPT, D = C::D;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* exp_base = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(exp_base + ES * C::kExpStage);
+  uint64_t* exp_full = bars;
+  uint64_t* exp_empty = bars + ES;
+  uint64_t* tmem_full = bars + 2 * ES;  // [2]
+  uint64_t* tmem_empty = tmem_full + 2;  // [2]
+  uint64_t* mma_done = tmem_full + 4;    // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = p.tiles_i * p.tiles_j;
+  const int kb_n = p.kblocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ES; ++s) {
+      mbar_init(&exp_full[s], kExpandWarps);
+      mbar_init(&exp_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_i8(128, BN);
+      int g = 0, t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++t) {
+        const int acc = t & 1, use = t >> 1;
+        if (use > 0 && !mbar_wait(&tmem_empty[acc], (use - 1) & 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kb_n; ++kb, ++g) {
+          const int s = g % ES;
+          if (!mbar_wait(&exp_full[s], (g / ES) & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t aP = smem_u32(exp_base + s * C::kExpStage);
+          const uint64_t da = umma_desc_sw128(aP);
+          const uint64_t db = umma_desc_sw128(aP + C::kExpP);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_i8_ss(d, da + 2 * kk, db + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&exp_empty[s]);
+        }
+        if (ok) umma_commit(&tmem_full[acc]);
+      }
+      umma_commit(mma_done);
+    }
+  } else if (warp >= 5) {
+    // ------------------------------------------------ load + expand (8 warps)
+    const int et = threadIdx.x - 5 * 32;
+    const int my_tiles = (ntiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                         static_cast<int>(gridDim.x);
+    const int total = my_tiles > 0 ? my_tiles * kb_n : 0;
+    // per-thread chunk coordinates (fixed across K blocks): row within P/Q and 16-byte column
+    auto load = [&](int g, uint4 (&w)[UPT]) {
+      if (g >= total) return;
+      const int tl = g / kb_n, kb = g - tl * kb_n;
+      const int tile = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
+      const int ti = tile % p.tiles_i, tj = tile / p.tiles_i;
+#pragma unroll
+      for (int i = 0; i < UPT; ++i) {
+        const int u = et + i * kExpandThreads;
+        const int row = u >> 2, c = u & 3;
+        const int kbyte = kb * 64 + c * 16;
+        const bool inP = i * kExpandThreads < 128 * 4;  // compile-time per i
+        const int grow = inP ? ti * 128 + row : tj * BN + (row - 128);
+        const bool valid = (inP ? grow < p.rowsP : grow < p.rowsQ) && kbyte < p.kbytes;
+        const uint8_t* base = inP ? p.P : p.Q;
+        w[i] = valid ? ldg_nc_v4(base + static_cast<int64_t>(grow) * p.kbytes + kbyte) : make_uint4(0, 0, 0, 0);
+      }
+    };
+    auto expand = [&](int g, const uint4 (&w)[UPT]) -> bool {
+      const int es = g % ES;
+      if (g >= ES && !mbar_wait(&exp_empty[es], ((g / ES) & 1u) ^ 1u, abort_flag)) return false;
+      uint8_t* dstP = exp_base + es * C::kExpStage;
+#pragma unroll
+      for (int i = 0; i < UPT; ++i) {
+        const int u = et + i * kExpandThreads;
+        const int row = u >> 2;
+        if (i * kExpandThreads < 128 * 4)
+          expand_chunk(w[i], dstP, row, u & 3);
+        else
+          expand_chunk(w[i], dstP + C::kExpP, row - 128, u & 3);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&exp_full[es]);
+      return true;
+    };
+    uint4 w0[UPT], w1[UPT], w2[UPT];
+    static_assert(D == 3, "register ring is unrolled for three K blocks");
+    load(0, w0);
+    load(1, w1);
+    load(2, w2);
+    for (int g = 0; g < total; g += 3) {
+      if (!expand(g, w0)) break;
+      load(g + 3, w0);
+      if (g + 1 >= total) break;
+      if (!expand(g + 1, w1)) break;
+      load(g + 4, w1);
+      if (g + 2 >= total) break;
+      if (!expand(g + 2, w2)) break;
+      load(g + 5, w2);
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 0-3)
+    const int row_local = warp * 32 + lane;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t) {
+      const int acc_i = t & 1, use = t >> 1;
+      bool ok = mbar_wait(&tmem_full[acc_i], use & 1u, abort_flag);
+      ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      const int ti = tile % p.tiles_i, tj = tile / p.tiles_i;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(acc_i * BN);
+      for (int j0 = 0; j0 < BN; j0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_row + j0, r);
+        tmem_ld_wait();
+        int32_t acc[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) acc[q] = static_cast<int32_t>(r[q]) >> 8;
+        epilogue16<BN, false>(p, ti, tj, row_local, j0, acc);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[acc_i]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    if (lane == 0) mbar_wait(mma_done, 0, nullptr);
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
