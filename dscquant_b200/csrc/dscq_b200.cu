@@ -137,8 +137,7 @@ cudaError_t launch_wht(const dscq::RowQuantParams& p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(dscq::wht_quant_pow2<LOGK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM);
   if (e != cudaSuccess) return e;
-  const int batches = (p.rows_out + C::ROWS - 1) / C::ROWS;
-  const unsigned grid = static_cast<unsigned>(std::min(batches, 2 * num_sms()));
+  const unsigned grid = static_cast<unsigned>((p.rows_out + C::ROWS - 1) / C::ROWS);
   dscq::wht_quant_pow2<LOGK><<<grid, C::THREADS, C::SMEM, st>>>(p);
   return cudaGetLastError();
 }
@@ -343,7 +342,7 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   DSCQ_REQUIRE(!zx || sums, "asymmetric activations (zx) need weight code sums");
   DSCQ_REQUIRE(out_dtype == DSCQ_BF16 || out_dtype == DSCQ_F16 || out_dtype == DSCQ_F32, "out_dtype must be bf16/f16/f32");
   DSCQ_REQUIRE(aligned(a, 16) && aligned(b, 16), "packed operands must be 16-byte aligned");
-  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_LARGE_M_TMA, "unknown GEMM variant");
+  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_LARGE_M_DIRECT, "unknown GEMM variant");
   int st = check_device(nullptr);
   if (st) return st;
 
@@ -411,9 +410,10 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   gp.rowsQ = static_cast<int>(rowsQ);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (persistent && variant == DSCQ_GEMM_LARGE_M_TMA)
+  if (persistent && variant == DSCQ_GEMM_LARGE_M_DIRECT)
+    return BN == 256 ? launch_gemm_ldg<256>(gp, s) : launch_gemm_ldg<128>(gp, s);
+  if (persistent)
     return BN == 256 ? launch_gemm_persistent<256>(tmP, tmQ, gp, s) : launch_gemm_persistent<128>(tmP, tmQ, gp, s);
-  if (persistent) return BN == 256 ? launch_gemm_ldg<256>(gp, s) : launch_gemm_ldg<128>(gp, s);
   if (swap) {
     if (BN == 16) return dispatch_split<16, true>(tmP, tmQ, gp, s);
     if (BN == 32) return dispatch_split<32, true>(tmP, tmQ, gp, s);

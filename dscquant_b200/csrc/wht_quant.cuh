@@ -2,13 +2,10 @@
 // for K = 2^LOGK (LOGK = 10..13), bf16 input. One HBM read of x, one write of
 // the packed codes (+ 4 B of scale per row): 2.5 B per element.
 //
-//   stage    persistent CTAs walk batches of ROWS rows; the next batch is
-//            copied into a shared-memory staging buffer with cp.async while
-//            the current one is computed (loads overlap all the arithmetic)
-//   phase 1  each thread reads E contiguous elements from the staging buffer,
-//            runs the butterflies over index bits [0, log2 E) in registers
-//            (packed f32x2 adds), and stores them to shared memory
-//            (XOR-swizzled 16-byte chunks: conflict-free stores and loads)
+//   phase 1  each thread loads E contiguous elements (16-byte loads), runs the
+//            butterflies over index bits [0, log2 E) in registers (packed
+//            f32x2 adds), and stores them to shared memory (XOR-swizzled
+//            16-byte chunks: conflict-free stores and column loads)
 //   phase 2  each thread reads GPT adjacent columns g.. of the row's
 //            [G x E] shared-memory matrix and runs the remaining butterflies
 //            over the G = K/E elements of each column in registers
@@ -37,9 +34,7 @@ struct WhtCfg {
   static constexpr int GPT = E / G;   // adjacent columns per thread in phase 2
   static constexpr int THREADS = 128;
   static constexpr int ROWS = THREADS / TR;
-  static constexpr int XCH = ROWS * K * 4;    // fp32 transpose buffer
-  static constexpr int STG = ROWS * K * 2;    // bf16 staging buffer
-  static constexpr int SMEM = XCH + STG;
+  static constexpr int SMEM = ROWS * K * 4;
   static_assert(LOGK >= 10 && LOGK <= 13, "K = 1024 .. 8192");
   static_assert(GPT == 2 || GPT == 4, "phase 2 needs 2 or 4 adjacent columns per thread");
   static_assert(TR <= THREADS && THREADS % TR == 0, "rows must tile the CTA");
@@ -52,65 +47,38 @@ __device__ __forceinline__ float2 bf16x2_to_f2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
 
-__device__ __forceinline__ void wq_cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-
 template <int LOGK>
 __global__ void __launch_bounds__(128) wht_quant_pow2(const RowQuantParams p) {
   using C = WhtCfg<LOGK>;
   constexpr int E = C::E, TR = C::TR, G = C::G, GPT = C::GPT, K = C::K;
-  constexpr int CM = E / 4 - 1;   // fp32 chunk swizzle mask
-  constexpr int SQ = E / 8;       // 16-byte bf16 chunks per thread segment
+  constexpr int CM = E / 4 - 1;  // chunk swizzle mask
   extern __shared__ float4 smem_f4[];
   float* sbase = reinterpret_cast<float*>(smem_f4);
-  uint8_t* stg = reinterpret_cast<uint8_t*>(smem_f4) + C::XCH;
   __shared__ float s_red[C::ROWS][2];
   __shared__ int s_sum[C::ROWS][2];
 
   const int r_local = threadIdx.x / TR;
   const int t = threadIdx.x % TR;
-  float* sb = sbase + r_local * K;
-  const int nbatch = (p.rows_out + C::ROWS - 1) / C::ROWS;
-
-  // staging layout: row r, thread segment t' (E bf16 = SQ chunks), chunk q at (q ^ (t' & (SQ-1)))
-  auto prefetch = [&](int b) {
-    const uint32_t base = smem_u32(stg);
-    for (int c = threadIdx.x; c < C::ROWS * K / 8; c += C::THREADS) {
-      const int r = c / (K / 8), cc = c % (K / 8);
-      const int ts = cc / SQ, q = cc % SQ;
-      const int row = b * C::ROWS + r;
-      if (row < p.M)
-        wq_cp_async16(base + r * K * 2 + ts * E * 2 + ((q ^ (ts & (SQ - 1))) << 4),
-                      reinterpret_cast<const __nv_bfloat16*>(p.x) + static_cast<int64_t>(row) * p.ld_x + cc * 8);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-
-  if (static_cast<int>(blockIdx.x) < nbatch) prefetch(blockIdx.x);
-  for (int b = blockIdx.x; b < nbatch; b += gridDim.x) {
-  const int row = b * C::ROWS + r_local;
+  const int row = blockIdx.x * C::ROWS + r_local;
   const bool live = row < p.M;
   const bool active = row < p.rows_out;
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-  __syncthreads();
+  float* sb = sbase + r_local * K;
 
   // ---------------- phase 1: contiguous E elements, butterflies over bits [0, LE)
   float2 V[E / 2];
   {
-    const uint8_t* seg = stg + r_local * K * 2 + t * E * 2;
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) +
+                                                      static_cast<int64_t>(live ? row : 0) * p.ld_x) +
+                       t * (E / 8);
 #pragma unroll
-    for (int q = 0; q < SQ; ++q) {
-      const uint4 w = live ? *reinterpret_cast<const uint4*>(seg + ((q ^ (t & (SQ - 1))) << 4))
-                           : make_uint4(0, 0, 0, 0);
+    for (int q = 0; q < E / 8; ++q) {
+      const uint4 w = live ? __ldcs(src + q) : make_uint4(0, 0, 0, 0);
       V[4 * q + 0] = bf16x2_to_f2(w.x);
       V[4 * q + 1] = bf16x2_to_f2(w.y);
       V[4 * q + 2] = bf16x2_to_f2(w.z);
       V[4 * q + 3] = bf16x2_to_f2(w.w);
     }
   }
-  __syncthreads();  // staging buffer consumed: start the next batch's copy
-  if (b + static_cast<int>(gridDim.x) < nbatch) prefetch(b + gridDim.x);
 #pragma unroll
   for (int m = 0; m < E / 2; ++m) V[m] = make_float2(V[m].x + V[m].y, V[m].x - V[m].y);
 #pragma unroll
@@ -118,9 +86,9 @@ __global__ void __launch_bounds__(128) wht_quant_pow2(const RowQuantParams p) {
 #pragma unroll
     for (int m = 0; m < E / 2; ++m) {
       if (!(m & hv)) {
-        const float2 a = V[m], b2 = V[m + hv];
-        V[m] = f2add(a, b2);
-        V[m + hv] = f2sub(a, b2);
+        const float2 a = V[m], b = V[m + hv];
+        V[m] = f2add(a, b);
+        V[m + hv] = f2sub(a, b);
       }
     }
   }
@@ -225,8 +193,6 @@ __global__ void __launch_bounds__(128) wht_quant_pow2(const RowQuantParams p) {
     }
     if (t == 0 && active) p.row_sums[row] = csum;
   }
-  }  // batch loop
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 }  // namespace dscq

@@ -42,7 +42,7 @@ extern "C" {
 #define DSCQ_GEMM_AUTO 0
 #define DSCQ_GEMM_SMALL_M 1     /* weights on the 128-row MMA side, tokens as MMA N */
 #define DSCQ_GEMM_LARGE_M 2     /* activations on the 128-row MMA side              */
-#define DSCQ_GEMM_LARGE_M_TMA 3 /* as LARGE_M, operands staged by TMA (A/B timing)    */
+#define DSCQ_GEMM_LARGE_M_DIRECT 3 /* as LARGE_M, operands loaded to registers (A/B timing) */
 
 int dscq_version(void);
 const char* dscq_last_error(void);
