@@ -181,6 +181,31 @@ int launch_gemm_ldg(const dscq::GemmParams& gp, cudaStream_t stream) {
   return DSCQ_OK;
 }
 
+int launch_gemm_pair(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq::GemmParams& gp,
+                     cudaStream_t stream) {
+  using C = dscq::PairCfg;
+  auto kern = dscq::w4a4_gemm_pair;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a4_gemm_pair)");
+  const int tiles = ((gp.M + 255) / 256) * gp.tiles_j;
+  const int pairs = std::min(tiles, num_sms() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(dscq::kGemmThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, tmP, tmQ, gp);
+  if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_pair");
+  return DSCQ_OK;
+}
+
 template <int BN, bool SWAP>
 int dispatch_split(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq::GemmParams& gp,
                    cudaStream_t stream) {
@@ -342,7 +367,7 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   DSCQ_REQUIRE(!zx || sums, "asymmetric activations (zx) need weight code sums");
   DSCQ_REQUIRE(out_dtype == DSCQ_BF16 || out_dtype == DSCQ_F16 || out_dtype == DSCQ_F32, "out_dtype must be bf16/f16/f32");
   DSCQ_REQUIRE(aligned(a, 16) && aligned(b, 16), "packed operands must be 16-byte aligned");
-  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_LARGE_M_DIRECT, "unknown GEMM variant");
+  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_LARGE_M_PAIR, "unknown GEMM variant");
   int st = check_device(nullptr);
   if (st) return st;
 
@@ -383,7 +408,8 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   const int64_t rowsP = swap ? N : M, rowsQ = swap ? M : N;
   st = make_u8_map(&tmP, P, rowsP, kbytes, kbytes, 128);
   if (st) return st;
-  st = make_u8_map(&tmQ, Q, rowsQ, kbytes, kbytes, BN);
+  const bool pair = persistent && BN == 256 && variant == DSCQ_GEMM_LARGE_M_PAIR;
+  st = make_u8_map(&tmQ, Q, rowsQ, kbytes, kbytes, pair ? 128 : BN);
   if (st) return st;
 
   dscq::GemmParams gp;
@@ -410,6 +436,7 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   gp.rowsQ = static_cast<int>(rowsQ);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (pair) return launch_gemm_pair(tmP, tmQ, gp, s);
   if (persistent && variant == DSCQ_GEMM_LARGE_M_DIRECT)
     return BN == 256 ? launch_gemm_ldg<256>(gp, s) : launch_gemm_ldg<128>(gp, s);
   if (persistent)

@@ -566,6 +566,231 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ============================================================ persistent, CTA pairs
+// Tile 256 x 256 computed by the two CTAs of a cluster pair with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32 per instruction). CTA r
+// of the pair stages, expands and holds rows [128r, 128r+128) of the A tile
+// and rows [128r, 128r+128) of the B tile; its TMEM receives rows
+// [128r, 128r+128) x all 256 columns of the accumulator. Per SM this halves
+// the B-operand bytes that TMA writes, the expansion reads and writes, and
+// the tensor cores read from shared memory, for the same MMA throughput.
+// Only the leader (rank 0) issues MMAs. Both CTAs' expansion warps arrive on
+// the leader's `exp_full` (the peer through its cluster address); the
+// leader's commits arrive on `exp_empty`, `tmem_full` and `mma_done` of both
+// CTAs; both CTAs' epilogue warps arrive on the leader's `tmem_empty`.
+//   warps 0-3 epilogue, warp 4 TMEM allocator (+ MMA issuer in the leader),
+//   warp 5 TMA producer, warps 6-13 expansion.
+struct PairCfg {
+  static constexpr int BN = 256;                    // pair tile N (128 B rows per CTA)
+  static constexpr int kRows = 256;                 // 128 A rows + 128 B rows per CTA
+  static constexpr int kRawStage = kRows * 64;      // 16 KB
+  static constexpr int kExpHalf = 128 * 128;        // 16 KB
+  static constexpr int kExpStage = kRows * 128;     // 32 KB
+  static constexpr int ES = 4;
+  static constexpr int RS = 5;
+  static constexpr int UPT = kRows * 4 / kExpandThreads;
+  static constexpr int kTmemCols = 2 * BN;          // two accumulators x 256 columns
+  static constexpr int kBarBytes = (2 * RS + 2 * ES + 5) * 8 + 16;
+  static constexpr int kSmemBytes = 1024 + ES * kExpStage + RS * kRawStage + kBarBytes;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    w4a4_gemm_pair(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
+                   const GemmParams p) {
+  using C = PairCfg;
+  constexpr int RS = C::RS, ES = C::ES, BN = C::BN;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* exp_base = smem;
+  uint8_t* raw_base = smem + ES * C::kExpStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw_base + RS * C::kRawStage);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = bars + RS;
+  uint64_t* exp_full = bars + 2 * RS;            // leader: 2 x 8 expansion warps
+  uint64_t* exp_empty = bars + 2 * RS + ES;      // both: leader's MMA commit
+  uint64_t* tmem_full = bars + 2 * RS + 2 * ES;  // [2] both: leader's MMA commit
+  uint64_t* tmem_empty = tmem_full + 2;          // [2] leader: 2 x 4 epilogue warps
+  uint64_t* mma_done = tmem_full + 4;            // [1] both
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x) >> 1, npairs = static_cast<int>(gridDim.x) >> 1;
+  const int tiles_i2 = (p.M + 255) / 256;
+  const int ntiles = tiles_i2 * p.tiles_j;
+  const int kb_n = p.kblocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], kExpandWarps);
+    }
+    for (int s = 0; s < ES; ++s) {
+      mbar_init(&exp_full[s], 2 * kExpandWarps);
+      mbar_init(&exp_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 8);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5 && lane == 0) {
+    tma_prefetch_desc(&tmP);
+    tma_prefetch_desc(&tmQ);
+  }
+  if (warp == 4) {
+    tmem_alloc_pair(tmem_slot, C::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM of the pair allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // leader's barriers as seen from this CTA (cluster addresses)
+  const uint32_t exp_full_ldr = dsmem_map(smem_u32(exp_full), 0);
+  const uint32_t tmem_empty_ldr = dsmem_map(smem_u32(tmem_empty), 0);
+
+  if (warp == 5) {
+    // ------------------------------------------------ TMA producer (both CTAs, own halves)
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < ntiles; tile += npairs) {
+        const int ti2 = tile % tiles_i2, tj = tile / tiles_i2;
+        for (int kb = 0; kb < kb_n; ++kb, ++g) {
+          const int s = g % RS;
+          if (g >= RS && !mbar_wait(&raw_empty[s], ((g / RS) & 1u) ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&raw_full[s], C::kRawStage);
+          uint8_t* dst = raw_base + s * C::kRawStage;
+          tma_load_2d(dst, &tmP, &raw_full[s], kb * 64, ti2 * 256 + static_cast<int>(rank) * 128);
+          tma_load_2d(dst + 128 * 64, &tmQ, &raw_full[s], kb * 64, tj * BN + static_cast<int>(rank) * 128);
+        }
+      }
+      if (!ok) {
+        for (int j = g > RS ? g - RS : 0; j < g; ++j) mbar_wait(&raw_full[j % RS], (j / RS) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_i8(256, BN);
+      const uint32_t exp_empty_peer = dsmem_map(smem_u32(exp_empty), 1);
+      const uint32_t tmem_full_peer = dsmem_map(smem_u32(tmem_full), 1);
+      int g = 0, t = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < ntiles; tile += npairs, ++t) {
+        const int acc = t & 1, use = t >> 1;
+        if (use > 0 && !mbar_wait_cluster(&tmem_empty[acc], (use - 1) & 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kb_n; ++kb, ++g) {
+          const int s = g % ES;
+          if (!mbar_wait_cluster(&exp_full[s], (g / ES) & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t aP = smem_u32(exp_base + s * C::kExpStage);
+          const uint64_t da = umma_desc_sw128(aP);
+          const uint64_t db = umma_desc_sw128(aP + C::kExpHalf);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_i8_ss_pair(d, da + 2 * kk, db + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_pair(smem_u32(&exp_empty[s]));
+          umma_commit_pair(exp_empty_peer + static_cast<uint32_t>(s * 8));
+        }
+        if (ok) {
+          umma_commit_pair(smem_u32(&tmem_full[acc]));
+          umma_commit_pair(tmem_full_peer + static_cast<uint32_t>(acc * 8));
+        }
+      }
+      umma_commit_pair(smem_u32(mma_done));
+      umma_commit_pair(dsmem_map(smem_u32(mma_done), 1));
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------ int4 -> int8 expansion (both CTAs)
+    const int et = threadIdx.x - 6 * 32;
+    int g = 0;
+    bool ok = true;
+    for (int tile = pair; ok && tile < ntiles; tile += npairs) {
+      for (int kb = 0; kb < kb_n; ++kb, ++g) {
+        const int rs = g % RS, es = g % ES;
+        if (!mbar_wait(&raw_full[rs], (g / RS) & 1u, abort_flag) ||
+            (g >= ES && !mbar_wait_cluster(&exp_empty[es], ((g / ES) & 1u) ^ 1u, abort_flag))) {
+          ok = false;
+          break;
+        }
+        const uint8_t* src = raw_base + rs * C::kRawStage;
+        uint8_t* dstA = exp_base + es * C::kExpStage;
+        uint4 w[C::UPT];
+#pragma unroll
+        for (int i = 0; i < C::UPT; ++i) w[i] = *reinterpret_cast<const uint4*>(src + (et + i * kExpandThreads) * 16);
+#pragma unroll
+        for (int i = 0; i < C::UPT; ++i) {
+          const int u = et + i * kExpandThreads;
+          const int row = u >> 2;
+          if (i * kExpandThreads < 128 * 4)
+            expand_chunk(w[i], dstA, row, u & 3);
+          else
+            expand_chunk(w[i], dstA + C::kExpHalf, row - 128, u & 3);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&raw_empty[rs]);
+          mbar_arrive_cluster(exp_full_ldr + static_cast<uint32_t>(es * 8));
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 0-3, both CTAs)
+    const int row_local = warp * 32 + lane;
+    int t = 0;
+    for (int tile = pair; tile < ntiles; tile += npairs, ++t) {
+      const int acc_i = t & 1, use = t >> 1;
+      bool ok = mbar_wait_cluster(&tmem_full[acc_i], use & 1u, abort_flag);
+      ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      const int ti2 = tile % tiles_i2, tj = tile / tiles_i2;
+      const int ti = ti2 * 2 + static_cast<int>(rank);  // 128-row block of this CTA
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(acc_i * BN);
+      for (int j0 = 0; j0 < BN; j0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_row + j0, r);
+        tmem_ld_wait();
+        int32_t acc[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) acc[q] = static_cast<int32_t>(r[q]) >> 8;
+        epilogue16<BN, false>(p, ti, tj, row_local, j0, acc);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tmem_empty_ldr + static_cast<uint32_t>(acc_i * 8));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4 && lane == 0) mbar_wait_cluster(mma_done, 0, nullptr);  // the pair's MMAs into this CTA retired
+  __syncwarp();
+  cluster_sync();  // no CTA leaves while its peer may still address its shared memory
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::kTmemCols);
+  }
+}
+
 // ============================================================ persistent, direct loads
 // Same tile loop, TMEM double buffering and epilogue as w4a4_gemm_persistent,
 // but the expansion warps read the packed int4 bytes straight from L2 with
