@@ -161,7 +161,7 @@ int launch_gemm_persistent(const CUtensorMap& tmP, const CUtensorMap& tmQ, const
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a4_gemm_persistent)");
   const int tiles = gp.tiles_i * gp.tiles_j;
   const int grid = std::min(tiles, num_sms());
-  kern<<<grid, dscq::kGemmThreads, C::kSmemBytes, stream>>>(tmP, tmQ, gp);
+  kern<<<grid, dscq::kPersistThreads, C::kSmemBytes, stream>>>(tmP, tmQ, gp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_persistent");
   return DSCQ_OK;
@@ -191,7 +191,7 @@ int launch_gemm_pair(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq:
   const int pairs = std::min(tiles, num_sms() / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
-  cfg.blockDim = dim3(dscq::kGemmThreads);
+  cfg.blockDim = dim3(dscq::kPersistThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

@@ -29,11 +29,14 @@
 //       main loop of the next; raw (TMA) and expanded stages are counted
 //       separately (more raw stages in flight to cover load latency).
 //
-// Warp roles (448 threads, one CTA per SM):
+// Warp roles, one-tile kernel (448 threads, one CTA per SM):
 //   warps 0-3   epilogue   (warp w owns TMEM lanes 32w..32w+31 = tile rows)
 //   warp  4     TMA producer (one lane)
 //   warp  5     TMEM allocator + MMA issuer (one lane)
 //   warps 6-13  int4 -> int8 expansion (256 threads)
+// Persistent kernels (576 threads): warps 0-7 epilogue (two per TMEM lane
+// quadrant, each half of the columns), warps 8-9 TMA producer and MMA issuer,
+// warps 10-17 expansion.
 #pragma once
 #include "ptx.cuh"
 
@@ -163,6 +166,89 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int ti, int tj, 
           store_from_float(p.out, o, p.out_dtype, f);
         }
       }
+    }
+  }
+}
+
+// ============================================================ epilogue of the persistent kernels
+// Eight epilogue warps: warp e reads TMEM lanes 32*(e & 3).. (its quadrant of
+// tile rows) and columns [(e >> 2) * BN/2, +BN/2). The tile's channel scales,
+// bias and weight code sums are staged once per tile in shared memory
+// (double-buffered by tile parity); accumulators come out of TMEM 32 columns
+// per load.
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kPersistThreads = 576;  // 8 epilogue + 2 control + 8 expansion warps
+
+template <int BN>
+struct EpiStage {
+  float sw[2][BN];
+  float bias[2][BN];
+  int32_t wsum[2][BN];
+};
+
+template <int BN>
+__device__ __forceinline__ void epilogue_stage(const GemmParams& p, int tj, int par, EpiStage<BN>* st, int et) {
+  for (int i = et; i < BN; i += kEpiThreads) {
+    const int n = tj * BN + i;
+    const bool in = n < p.N;
+    st->sw[par][i] = in ? p.sw[n] : 0.f;
+    if (p.bias) st->bias[par][i] = in ? load_as_float(p.bias, n, p.out_dtype) : 0.f;
+    if (p.zx) st->wsum[par][i] = in ? p.wsum[n] : 0;
+  }
+}
+
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int tj, uint32_t tmem_acc, int ew, int lane,
+                                              const EpiStage<BN>* st, int par) {
+  const int q = ew & 3, h = ew >> 2;
+  const int row_local = q * 32 + lane;
+  const int m = ti * 128 + row_local;
+  const bool live = m < p.M;
+  const uint32_t t_row = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
+  const bool asym = p.zx != nullptr, has_bias = p.bias != nullptr, has_res = p.residual != nullptr;
+  const float sxm = live ? p.sx[m] : 0.f;
+  const int32_t zc = (asym && live) ? 8 - p.zx[m] : 0;
+#pragma unroll 1
+  for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 32) {
+    uint32_t r[32];
+    tmem_ld32(t_row + static_cast<uint32_t>(c0), r);
+    tmem_ld_wait();
+    if (!live) continue;
+    const int n0 = tj * BN + c0;
+    const int64_t o0 = static_cast<int64_t>(m) * p.N + n0;
+    const bool full = n0 + 32 <= p.N;
+    if (p.raw) {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (n0 + t < p.N) p.raw[o0 + t] = static_cast<int32_t>(r[t]) >> 8;
+    }
+    if (!p.out) continue;
+    float f[32];
+#pragma unroll
+    for (int t = 0; t < 32; ++t) {
+      int32_t a = static_cast<int32_t>(r[t]) >> 8;
+      if (asym) a += zc * st->wsum[par][c0 + t];
+      f[t] = epi_scale(a, sxm, st->sw[par][c0 + t]);
+      if (has_bias) f[t] = __fadd_rn(f[t], st->bias[par][c0 + t]);
+      if (has_res && (full || n0 + t < p.N)) f[t] = __fadd_rn(f[t], load_as_float(p.residual, o0 + t, p.out_dtype));
+    }
+    if (full && p.vec_out && p.out_dtype == kOutBF16) {
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + o0);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(f[8 * v + 2 * u], f[8 * v + 2 * u + 1]);
+          w[u] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (n0 + t < p.N) store_from_float(p.out, o0 + t, p.out_dtype, f[t]);
     }
   }
 }
@@ -379,7 +465,8 @@ struct PCfg {
   static constexpr int UPT = kRows * 4 / kExpandThreads;                         // 16-B chunks per thread
   static constexpr int kTmemCols = 2 * BN;                                       // two accumulators
   static constexpr int kBarBytes = (2 * RS + 2 * ES + 5) * 8 + 16;
-  static constexpr int kSmemBytes = 1024 + ES * kExpStage + RS * kRawStage + kBarBytes;
+  static constexpr int kEpiBytes = static_cast<int>(sizeof(EpiStage<BN>));
+  static constexpr int kSmemBytes = 1024 + ES * kExpStage + RS * kRawStage + kBarBytes + kEpiBytes;
   static_assert(BN == 128 || BN == 256, "persistent kernel uses N tiles of 128 or 256");
   static_assert(RS >= 2, "need two raw stages");
   static_assert(kRows * 4 % kExpandThreads == 0, "expansion chunks must divide evenly");
@@ -387,7 +474,7 @@ struct PCfg {
 };
 
 template <int BN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kPersistThreads, 1)
     w4a4_gemm_persistent(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                          const GemmParams p) {
   using C = PCfg<BN>;
@@ -406,6 +493,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* mma_done = tmem_full + 4;             // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  EpiStage<BN>* est = reinterpret_cast<EpiStage<BN>*>(reinterpret_cast<uint8_t*>(bars) + C::kBarBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = p.tiles_i * p.tiles_j;
@@ -422,17 +510,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 4);
+      mbar_init(&tmem_empty[a], kEpiWarps);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     tma_prefetch_desc(&tmP);
     tma_prefetch_desc(&tmQ);
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
@@ -441,7 +529,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       int g = 0;
@@ -464,7 +552,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int j = g > RS ? g - RS : 0; j < g; ++j) mbar_wait(&raw_full[j % RS], (j / RS) & 1u, nullptr);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_i8(128, BN);
@@ -494,9 +582,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       umma_commit(mma_done);
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 10) {
     // ------------------------------------------------ int4 -> int8 expansion
-    const int et = threadIdx.x - 6 * 32;
+    const int et = threadIdx.x - 10 * 32;
     int g = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
@@ -530,26 +618,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 0-3)
-    const int row_local = warp * 32 + lane;
+    // ------------------------------------------------ epilogue (warps 0-7)
     int t = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t) {
       const int acc_i = t & 1, use = t >> 1;
+      const int ti = tile % p.tiles_i, tj = tile / p.tiles_i;
+      epilogue_stage<BN>(p, tj, t & 1, est, threadIdx.x);
       bool ok = mbar_wait(&tmem_full[acc_i], use & 1u, abort_flag);
-      ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+      // staged scales become visible and all eight warps agree on continuing
+      ok = named_bar_and(1, kEpiThreads, ok && !*abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const int ti = tile % p.tiles_i, tj = tile / p.tiles_i;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(acc_i * BN);
-      for (int j0 = 0; j0 < BN; j0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(t_row + j0, r);
-        tmem_ld_wait();
-        int32_t acc[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) acc[q] = static_cast<int32_t>(r[q]) >> 8;
-        epilogue16<BN, false>(p, ti, tj, row_local, j0, acc);
-      }
+      epilogue_tile<BN>(p, ti, tj, tmem_base + static_cast<uint32_t>(acc_i * BN), warp, lane, est, t & 1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[acc_i]);
@@ -558,7 +638,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     if (lane == 0) mbar_wait(mma_done, 0, nullptr);  // every issued MMA has retired
     __syncwarp();
     tc_fence_after();
@@ -591,11 +671,12 @@ struct PairCfg {
   static constexpr int UPT = kRows * 4 / kExpandThreads;
   static constexpr int kTmemCols = 2 * BN;          // two accumulators x 256 columns
   static constexpr int kBarBytes = (2 * RS + 2 * ES + 5) * 8 + 16;
-  static constexpr int kSmemBytes = 1024 + ES * kExpStage + RS * kRawStage + kBarBytes;
+  static constexpr int kEpiBytes = static_cast<int>(sizeof(EpiStage<BN>));
+  static constexpr int kSmemBytes = 1024 + ES * kExpStage + RS * kRawStage + kBarBytes + kEpiBytes;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kPersistThreads, 1)
     w4a4_gemm_pair(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                    const GemmParams p) {
   using C = PairCfg;
@@ -614,6 +695,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* mma_done = tmem_full + 4;            // [1] both
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  EpiStage<BN>* est = reinterpret_cast<EpiStage<BN>*>(reinterpret_cast<uint8_t*>(bars) + C::kBarBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -634,17 +716,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 8);
+      mbar_init(&tmem_empty[a], 2 * kEpiWarps);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5 && lane == 0) {
+  if (warp == 9 && lane == 0) {
     tma_prefetch_desc(&tmP);
     tma_prefetch_desc(&tmQ);
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc_pair(tmem_slot, C::kTmemCols);
     tmem_relinquish_pair();
   }
@@ -657,7 +739,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t exp_full_ldr = dsmem_map(smem_u32(exp_full), 0);
   const uint32_t tmem_empty_ldr = dsmem_map(smem_u32(tmem_empty), 0);
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ------------------------------------------------ TMA producer (both CTAs, own halves)
     if (lane == 0) {
       int g = 0;
@@ -680,7 +762,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int j = g > RS ? g - RS : 0; j < g; ++j) mbar_wait(&raw_full[j % RS], (j / RS) & 1u, nullptr);
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
       constexpr uint32_t idesc = umma_idesc_i8(256, BN);
@@ -717,9 +799,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       umma_commit_pair(smem_u32(mma_done));
       umma_commit_pair(dsmem_map(smem_u32(mma_done), 1));
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 10) {
     // ------------------------------------------------ int4 -> int8 expansion (both CTAs)
-    const int et = threadIdx.x - 6 * 32;
+    const int et = threadIdx.x - 10 * 32;
     int g = 0;
     bool ok = true;
     for (int tile = pair; ok && tile < ntiles; tile += npairs) {
@@ -753,27 +835,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 0-3, both CTAs)
-    const int row_local = warp * 32 + lane;
+    // ------------------------------------------------ epilogue (warps 0-7, both CTAs)
     int t = 0;
     for (int tile = pair; tile < ntiles; tile += npairs, ++t) {
       const int acc_i = t & 1, use = t >> 1;
-      bool ok = mbar_wait_cluster(&tmem_full[acc_i], use & 1u, abort_flag);
-      ok = __all_sync(0xffffffffu, ok && !*abort_flag);
-      if (!ok) break;
-      tc_fence_after();
       const int ti2 = tile % tiles_i2, tj = tile / tiles_i2;
       const int ti = ti2 * 2 + static_cast<int>(rank);  // 128-row block of this CTA
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(acc_i * BN);
-      for (int j0 = 0; j0 < BN; j0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(t_row + j0, r);
-        tmem_ld_wait();
-        int32_t acc[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) acc[q] = static_cast<int32_t>(r[q]) >> 8;
-        epilogue16<BN, false>(p, ti, tj, row_local, j0, acc);
-      }
+      epilogue_stage<BN>(p, tj, t & 1, est, threadIdx.x);
+      bool ok = mbar_wait_cluster(&tmem_full[acc_i], use & 1u, abort_flag);
+      ok = named_bar_and(1, kEpiThreads, ok && !*abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      epilogue_tile<BN>(p, ti, tj, tmem_base + static_cast<uint32_t>(acc_i * BN), warp, lane, est, t & 1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tmem_empty_ldr + static_cast<uint32_t>(acc_i * 8));
@@ -782,10 +855,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4 && lane == 0) mbar_wait_cluster(mma_done, 0, nullptr);  // the pair's MMAs into this CTA retired
+  if (warp == 8 && lane == 0) mbar_wait_cluster(mma_done, 0, nullptr);  // the pair's MMAs into this CTA retired
   __syncwarp();
   cluster_sync();  // no CTA leaves while its peer may still address its shared memory
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, C::kTmemCols);
   }
