@@ -44,6 +44,10 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "llama2-70b-tp"],
+                   help="llama2-7b: config 1 layer, data parallel over tokens (default); "
+                        "llama2-70b-tp: config 4 layer, column-parallel over N with the fused all-gather")
+    p.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"])
     p.add_argument("--tokens", type=int, default=2048)
     p.add_argument("--replicas", type=int, default=4, help="layer replicas cycled so the working set exceeds L2")
     p.add_argument("--no-sweep", action="store_true")
@@ -218,6 +222,78 @@ def run_reference(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- config 4: column-parallel 70B layer
+LAYER70 = [("qkv", 8192, 10240), ("o", 8192, 8192), ("gate", 8192, 28672), ("up", 8192, 28672), ("down", 28672, 8192)]
+
+
+def run_tp(args) -> None:
+    """Llama-2-70B layer linears at M = 4096 tokens, column-parallel over N on every
+    rank of the job; the shards are exchanged inside the GEMM epilogue (fused) or by NCCL all-gather.
+    Strong scaling: the total work is fixed; value = layer ops / max-over-ranks step time."""
+    import datetime
+
+    import torch
+    import torch.distributed as tdist
+
+    from dscquant_b200 import _lib, ops, parallel, synthetic  # noqa: F401
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29531")
+    tdist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                             device_id=dev)
+    M = 4096
+    gen = torch.Generator(device=dev)
+    layers = []
+    for i, (name, K, N) in enumerate(LAYER70):
+        lo, hi = parallel.shard_bounds(N, world, rank)
+        gen.manual_seed(7000 + 31 * i + rank)
+        w = (torch.randn((hi - lo, K), generator=gen, device=dev, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+        layers.append((name, K, N, parallel.ColumnParallelQuantLinear(w, N, mode=args.tp_mode, max_tokens=M)))
+        del w
+    xs = {}
+    for K in sorted({k for _, k, _ in LAYER70}):
+        gen.manual_seed(9000 + K)
+        xs[K] = torch.randn((M, K), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for name, K, N, layer in layers:
+            layer(xs[K])
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    tdist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+    ms = float(t.item())
+    ops_ = float(sum(2 * M * n * k for _, k, n in LAYER70))
+    if rank == 0:
+        print(json.dumps({"metric": "W4A4 linear TOPS, Llama-2-70B layer linears, column-parallel over N",
+                          "value": ops_ / (ms * 1e-3) / 1e12, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+                          "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                          "vs_baseline": None, "dtype": "int4 x int4 -> int32 (bf16 in/out)",
+                          "data": "synthetic (seeded normal activations and weights)",
+                          "config": {"workload": "llama2-70b-tp", "tokens": M, "tp_mode": args.tp_mode,
+                                     "shapes_KxN": [[k, n] for _, k, n in LAYER70],
+                                     "parallelism": f"tp{world} column-parallel over N"}}), flush=True)
+    del layers
+    tdist.barrier()
+    tdist.destroy_process_group()
+
+
 # ---------------------------------------------------------------- GPU arm
 def main():
     args = parse()
@@ -227,6 +303,9 @@ def main():
     dist = world > 1 and "RANK" in os.environ
     if args.kernel_case:
         kernel_case(args)
+        return
+    if args.workload == "llama2-70b-tp" and args.impl == "ours":
+        run_tp(args)
         return
     if args.impl == "reference":
         if dist:

@@ -357,11 +357,16 @@ int dscq_quantize(const void* x, int x_dtype, int64_t M, int64_t K, float clip, 
                        zeros, nullptr, nullptr, 0, stream);
 }
 
-int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32_t* zx, const float* sw,
-                const int32_t* sums, const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP,
-                int out_dtype, void* out, int32_t* raw, int variant, void* stream) {
+static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, const int32_t* zx, const float* sw,
+                       const int32_t* sums, const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP,
+                       int out_dtype, void* const* outs, int n_outs, int64_t ld_out, int64_t col_off, int32_t* raw,
+                       int variant, void* stream) {
+  void* out = n_outs > 0 ? outs[0] : nullptr;
   DSCQ_REQUIRE(a && b && sx && sw, "a, b, sx and sw must not be null");
   DSCQ_REQUIRE(out || raw, "at least one of out / raw must be given");
+  DSCQ_REQUIRE(n_outs >= 0 && n_outs <= 8, "at most 8 output buffers");
+  for (int i = 0; i < n_outs; ++i) DSCQ_REQUIRE(outs[i] != nullptr, "output buffers must not be null");
+  DSCQ_REQUIRE(col_off >= 0 && ld_out >= col_off + N, "ld_out must cover col_off + N");
   DSCQ_REQUIRE(M > 0 && M <= (1 << 24) && N > 0 && N <= (1 << 24) && KP > 0 && KP <= 1048576 && KP % 64 == 0,
                "Invalid dimensions (need M, N > 0 and KP a positive multiple of 64)");
   DSCQ_REQUIRE(!zx || sums, "asymmetric activations (zx) need weight code sums");
@@ -428,7 +433,13 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   gp.out = out;
   gp.raw = raw;
   gp.out_dtype = out_dtype;
-  gp.vec_out = (out && aligned(out, 16) && (N % 8 == 0)) ? 1 : 0;
+  bool vec = out != nullptr && ld_out % 8 == 0 && col_off % 8 == 0;
+  for (int i = 0; i < n_outs; ++i) vec = vec && aligned(outs[i], 16);
+  gp.vec_out = vec ? 1 : 0;
+  gp.ld_out = ld_out;
+  gp.col_off = static_cast<int>(col_off);
+  gp.n_outs = n_outs;
+  for (int i = 0; i < 8; ++i) gp.outs[i] = i < n_outs ? outs[i] : nullptr;
   gp.P = P;
   gp.Q = Q;
   gp.kbytes = static_cast<int>(kbytes);
@@ -448,6 +459,23 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
   }
   if (BN == 256) return dispatch_split<256, false>(tmP, tmQ, gp, s);
   return dispatch_split<128, false>(tmP, tmQ, gp, s);
+}
+
+int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32_t* zx, const float* sw,
+                const int32_t* sums, const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP,
+                int out_dtype, void* out, int32_t* raw, int variant, void* stream) {
+  void* outs[1] = {out};
+  return matmul_impl(a, b, sx, zx, sw, sums, bias, residual, M, N, KP, out_dtype, outs, out ? 1 : 0, N, 0, raw, variant,
+                     stream);
+}
+
+int dscq_matmul_cols(const uint8_t* a, const uint8_t* b, const float* sx, const int32_t* zx, const float* sw,
+                     const int32_t* sums, const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP,
+                     int out_dtype, void* const* outs, int n_outs, int64_t ld_out, int64_t col_off, int variant,
+                     void* stream) {
+  DSCQ_REQUIRE(outs != nullptr && n_outs >= 1, "need at least one output buffer");
+  return matmul_impl(a, b, sx, zx, sw, sums, bias, residual, M, N, KP, out_dtype, outs, n_outs, ld_out, col_off,
+                     nullptr, variant, stream);
 }
 
 int dscq_pack_int4(const int8_t* codes, int64_t rows, int64_t K, int64_t ld_codes, uint8_t* packed,

@@ -64,6 +64,13 @@ struct GemmParams {
   const uint8_t* Q;
   int kbytes;
   int rowsP, rowsQ;
+  // output placement: out[m * ld_out + col_off + n] in every buffer outs[0..n_outs)
+  // (outs[0] == out; more than one buffer = the same tile stored to the peer
+  // GPUs of a column-parallel group). residual uses the same indexing.
+  int64_t ld_out;
+  int col_off;
+  int n_outs;
+  void* outs[8];
 };
 
 constexpr int kGemmThreads = 448;
@@ -114,12 +121,13 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int ti, int tj, 
     if (m >= p.M) return;
     const float sxm = p.sx[m];
     const int32_t zc = asym ? 8 - p.zx[m] : 0;
-    const int64_t o0 = static_cast<int64_t>(m) * p.N + n0;
+    const int64_t r0 = static_cast<int64_t>(m) * p.N + n0;                 // raw index
+    const int64_t o0 = static_cast<int64_t>(m) * p.ld_out + p.col_off + n0;  // out index
     const bool full = n0 + 16 <= p.N;
     if (p.raw) {
 #pragma unroll
       for (int t = 0; t < 16; ++t)
-        if (n0 + t < p.N) p.raw[o0 + t] = acc[t];
+        if (n0 + t < p.N) p.raw[r0 + t] = acc[t];
     }
     if (p.out) {
       float f[16];
@@ -137,13 +145,16 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int ti, int tj, 
           __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * t], f[2 * t + 1]);
           w[t] = *reinterpret_cast<uint32_t*>(&h2);
         }
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + o0);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        for (int b = 0; b < p.n_outs; ++b) {
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.outs[b]) + o0);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
       } else {
+        for (int b = 0; b < p.n_outs; ++b)
 #pragma unroll
-        for (int t = 0; t < 16; ++t)
-          if (n0 + t < p.N) store_from_float(p.out, o0 + t, p.out_dtype, f[t]);
+          for (int t = 0; t < 16; ++t)
+            if (n0 + t < p.N) store_from_float(p.outs[b], o0 + t, p.out_dtype, f[t]);
       }
     }
   } else {
@@ -156,14 +167,14 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int ti, int tj, 
     for (int t = 0; t < 16; ++t) {
       const int m = tj * BN + j0 + t;
       if (m < p.M) {
-        const int64_t o = static_cast<int64_t>(m) * p.N + n;
-        if (p.raw) p.raw[o] = acc[t];
+        const int64_t o = static_cast<int64_t>(m) * p.ld_out + p.col_off + n;
+        if (p.raw) p.raw[static_cast<int64_t>(m) * p.N + n] = acc[t];
         if (p.out) {
           const int32_t corr = asym ? acc[t] + (8 - p.zx[m]) * wsn : acc[t];
           float f = epi_scale(corr, p.sx[m], swn);
           if (has_bias) f = __fadd_rn(f, bn);
           if (has_res) f = __fadd_rn(f, load_as_float(p.residual, o, p.out_dtype));
-          store_from_float(p.out, o, p.out_dtype, f);
+          for (int b = 0; b < p.n_outs; ++b) store_from_float(p.outs[b], o, p.out_dtype, f);
         }
       }
     }
@@ -216,12 +227,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int t
     tmem_ld_wait();
     if (!live) continue;
     const int n0 = tj * BN + c0;
-    const int64_t o0 = static_cast<int64_t>(m) * p.N + n0;
+    const int64_t o0 = static_cast<int64_t>(m) * p.ld_out + p.col_off + n0;
     const bool full = n0 + 32 <= p.N;
     if (p.raw) {
+      const int64_t r0 = static_cast<int64_t>(m) * p.N + n0;
 #pragma unroll
       for (int t = 0; t < 32; ++t)
-        if (n0 + t < p.N) p.raw[o0 + t] = static_cast<int32_t>(r[t]) >> 8;
+        if (n0 + t < p.N) p.raw[r0 + t] = static_cast<int32_t>(r[t]) >> 8;
     }
     if (!p.out) continue;
     float f[32];
@@ -234,7 +246,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int t
       if (has_res && (full || n0 + t < p.N)) f[t] = __fadd_rn(f[t], load_as_float(p.residual, o0 + t, p.out_dtype));
     }
     if (full && p.vec_out && p.out_dtype == kOutBF16) {
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + o0);
+      uint4 vv[4];
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
         uint32_t w[4];
@@ -243,12 +255,18 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int t
           __nv_bfloat162 h2 = __floats2bfloat162_rn(f[8 * v + 2 * u], f[8 * v + 2 * u + 1]);
           w[u] = *reinterpret_cast<uint32_t*>(&h2);
         }
-        dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+        vv[v] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      for (int b = 0; b < p.n_outs; ++b) {
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.outs[b]) + o0);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) dst[v] = vv[v];
       }
     } else {
+      for (int b = 0; b < p.n_outs; ++b)
 #pragma unroll
-      for (int t = 0; t < 32; ++t)
-        if (n0 + t < p.N) store_from_float(p.out, o0 + t, p.out_dtype, f[t]);
+        for (int t = 0; t < 32; ++t)
+          if (n0 + t < p.N) store_from_float(p.outs[b], o0 + t, p.out_dtype, f[t]);
     }
   }
 }

@@ -106,6 +106,19 @@ int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32
                 const int32_t* sums, const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP,
                 int out_dtype, void* out, int32_t* raw, int variant, void* stream);
 
+/*
+ * Column-block form of dscq_matmul (no counterpart in the reference, which has
+ * no multi-GPU code): the [M, N] result is written at rows 0..M-1, columns
+ * col_off..col_off+N-1 of buffers with row stride ld_out elements, into each of
+ * the n_outs (1..8) buffers in `outs` -- in a column-parallel group, the same
+ * output buffer of every GPU (peer pointers), so the all-gather of the shards
+ * happens in the GEMM epilogue over NVLink. `residual` uses the same indexing.
+ */
+int dscq_matmul_cols(const uint8_t* a, const uint8_t* b, const float* sx, const int32_t* zx, const float* sw,
+                     const int32_t* sums, const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP,
+                     int out_dtype, void* const* outs, int n_outs, int64_t ld_out, int64_t col_off, int variant,
+                     void* stream);
+
 /* pack_int4, core/quantization.py:31-40. codes [rows, K] int8 (row stride
  * ld_codes) -> packed [rows, ceil(K/2)] (row stride ld_packed). Codes outside
  * [-8, 7] are counted into *bad_count (device int, caller-zeroed). */
