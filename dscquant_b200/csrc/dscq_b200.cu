@@ -16,6 +16,7 @@
 #include "rowquant.cuh"
 #include "wht_quant.cuh"
 #include "kron_quant.cuh"
+#include "gemv_w4a4.cuh"
 
 namespace {
 
@@ -206,6 +207,21 @@ int launch_gemm_pair(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq:
   return DSCQ_OK;
 }
 
+int launch_gemv(const dscq::GemmParams& gp, cudaStream_t stream) {
+  const unsigned grid = static_cast<unsigned>((gp.N + 15) / 16);
+  const int nt = (gp.M + 7) / 8;
+  const unsigned threads = dscq::kGemvWarps * 32;
+  if (nt <= 1)
+    dscq::w4a4_gemv<1><<<grid, threads, 0, stream>>>(gp);
+  else if (nt <= 2)
+    dscq::w4a4_gemv<2><<<grid, threads, 0, stream>>>(gp);
+  else
+    dscq::w4a4_gemv<4><<<grid, threads, 0, stream>>>(gp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemv");
+  return DSCQ_OK;
+}
+
 template <int BN, bool SWAP>
 int dispatch_split(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq::GemmParams& gp,
                    cudaStream_t stream) {
@@ -372,7 +388,7 @@ static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, cons
   DSCQ_REQUIRE(!zx || sums, "asymmetric activations (zx) need weight code sums");
   DSCQ_REQUIRE(out_dtype == DSCQ_BF16 || out_dtype == DSCQ_F16 || out_dtype == DSCQ_F32, "out_dtype must be bf16/f16/f32");
   DSCQ_REQUIRE(aligned(a, 16) && aligned(b, 16), "packed operands must be 16-byte aligned");
-  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_LARGE_M_PAIR, "unknown GEMM variant");
+  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_SMALL_M_TC, "unknown GEMM variant");
   int st = check_device(nullptr);
   if (st) return st;
 
@@ -380,7 +396,9 @@ static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, cons
     return fail(DSCQ_ERR_UNSUPPORTED, "KP > 65536: the int8 tensor-core accumulation (256 * sum) would overflow int32");
   const int64_t kbytes = KP / 2;
   const int kblocks = static_cast<int>((KP + 127) / 128);
-  const bool swap = variant == DSCQ_GEMM_SMALL_M || (variant == DSCQ_GEMM_AUTO && M <= 64);
+  const bool decode = M <= 32 && (variant == DSCQ_GEMM_AUTO || variant == DSCQ_GEMM_SMALL_M);
+  const bool swap = variant == DSCQ_GEMM_SMALL_M || variant == DSCQ_GEMM_SMALL_M_TC ||
+                    (variant == DSCQ_GEMM_AUTO && M <= 64);
   const int nsm = num_sms();
   int BN;
   int64_t ti, tj;
@@ -447,6 +465,11 @@ static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, cons
   gp.rowsQ = static_cast<int>(rowsQ);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (decode) {
+    gp.P = a;  // activations
+    gp.Q = b;  // weights
+    return launch_gemv(gp, s);
+  }
   if (pair) return launch_gemm_pair(tmP, tmQ, gp, s);
   if (persistent && variant == DSCQ_GEMM_LARGE_M_DIRECT)
     return BN == 256 ? launch_gemm_ldg<256>(gp, s) : launch_gemm_ldg<128>(gp, s);

@@ -40,10 +40,11 @@ extern "C" {
 
 /* GEMM variants (dscq_matmul `variant`) */
 #define DSCQ_GEMM_AUTO 0
-#define DSCQ_GEMM_SMALL_M 1     /* weights on the 128-row MMA side, tokens as MMA N */
+#define DSCQ_GEMM_SMALL_M 1     /* decode kernel for M <= 32, else the SMALL_M_TC path */
 #define DSCQ_GEMM_LARGE_M 2     /* activations on the 128-row MMA side              */
 #define DSCQ_GEMM_LARGE_M_DIRECT 3 /* as LARGE_M, operands loaded to registers (A/B timing) */
 #define DSCQ_GEMM_LARGE_M_PAIR 4   /* as LARGE_M, 256x256 tiles on CTA pairs (cta_group::2)  */
+#define DSCQ_GEMM_SMALL_M_TC 5     /* tcgen05 with weights on the 128-row MMA side (tokens as MMA N) */
 
 int dscq_version(void);
 const char* dscq_last_error(void);

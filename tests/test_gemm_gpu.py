@@ -67,8 +67,9 @@ def test_gemm_exact_auto(oracle, cuda_device, M, N, KP):
     _run(oracle, cuda_device, M, N, KP)
 
 
-@pytest.mark.parametrize("variant", ["small_m", "large_m"])
-@pytest.mark.parametrize("M,N,KP", [(1, 128, 128), (20, 200, 256), (64, 384, 1024), (130, 260, 192), (256, 256, 4096)])
+@pytest.mark.parametrize("variant", ["small_m", "small_m_tc", "large_m"])
+@pytest.mark.parametrize("M,N,KP", [(1, 128, 128), (20, 200, 256), (64, 384, 1024), (130, 260, 192), (256, 256, 4096),
+                                    (3, 4096, 11008 // 64 * 64 + 64), (32, 1000, 1472), (17, 333, 64)])
 def test_gemm_exact_forced_variant(oracle, cuda_device, variant, M, N, KP):
     _run(oracle, cuda_device, M, N, KP, variant=variant)
 
@@ -86,7 +87,7 @@ def test_gemm_persistent_epilogue_options(oracle, cuda_device, variant):
     _run(oracle, cuda_device, 640, 2304, 512, variant=variant, asym=True, bias=True, residual=True)
 
 
-@pytest.mark.parametrize("M,N,KP", [(5, 96, 128), (100, 200, 256)])
+@pytest.mark.parametrize("M,N,KP", [(5, 96, 128), (100, 200, 256), (24, 136, 4096)])
 def test_gemm_asym_bias_residual(oracle, cuda_device, M, N, KP):
     _run(oracle, cuda_device, M, N, KP, asym=True, bias=True, residual=True)
 
