@@ -185,7 +185,7 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int ti, int tj, 
 // Eight epilogue warps: warp e reads TMEM lanes 32*(e & 3).. (its quadrant of
 // tile rows) and columns [(e >> 2) * BN/2, +BN/2). The tile's channel scales,
 // bias and weight code sums are staged once per tile in shared memory
-// (double-buffered by tile parity); accumulators come out of TMEM 32 columns
+// (double-buffered by tile parity); accumulators come out of TMEM 16 columns
 // per load.
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
@@ -221,24 +221,24 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int t
   const float sxm = live ? p.sx[m] : 0.f;
   const int32_t zc = (asym && live) ? 8 - p.zx[m] : 0;
 #pragma unroll 1
-  for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 32) {
-    uint32_t r[32];
-    tmem_ld32(t_row + static_cast<uint32_t>(c0), r);
+  for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 16) {
+    uint32_t r[16];
+    tmem_ld16(t_row + static_cast<uint32_t>(c0), r);
     tmem_ld_wait();
     if (!live) continue;
     const int n0 = tj * BN + c0;
     const int64_t o0 = static_cast<int64_t>(m) * p.ld_out + p.col_off + n0;
-    const bool full = n0 + 32 <= p.N;
+    const bool full = n0 + 16 <= p.N;
     if (p.raw) {
       const int64_t r0 = static_cast<int64_t>(m) * p.N + n0;
 #pragma unroll
-      for (int t = 0; t < 32; ++t)
+      for (int t = 0; t < 16; ++t)
         if (n0 + t < p.N) p.raw[r0 + t] = static_cast<int32_t>(r[t]) >> 8;
     }
     if (!p.out) continue;
-    float f[32];
+    float f[16];
 #pragma unroll
-    for (int t = 0; t < 32; ++t) {
+    for (int t = 0; t < 16; ++t) {
       int32_t a = static_cast<int32_t>(r[t]) >> 8;
       if (asym) a += zc * st->wsum[par][c0 + t];
       f[t] = epi_scale(a, sxm, st->sw[par][c0 + t]);
@@ -246,9 +246,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int t
       if (has_res && (full || n0 + t < p.N)) f[t] = __fadd_rn(f[t], load_as_float(p.residual, o0 + t, p.out_dtype));
     }
     if (full && p.vec_out && p.out_dtype == kOutBF16) {
-      uint4 vv[4];
+      uint4 vv[2];
 #pragma unroll
-      for (int v = 0; v < 4; ++v) {
+      for (int v = 0; v < 2; ++v) {
         uint32_t w[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -259,13 +259,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int t
       }
       for (int b = 0; b < p.n_outs; ++b) {
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.outs[b]) + o0);
-#pragma unroll
-        for (int v = 0; v < 4; ++v) dst[v] = vv[v];
+        dst[0] = vv[0];
+        dst[1] = vv[1];
       }
     } else {
       for (int b = 0; b < p.n_outs; ++b)
 #pragma unroll
-        for (int t = 0; t < 32; ++t)
+        for (int t = 0; t < 16; ++t)
           if (n0 + t < p.N) store_from_float(p.outs[b], o0 + t, p.out_dtype, f[t]);
     }
   }
@@ -885,23 +885,24 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
 // ============================================================ persistent, direct loads
 // Same tile loop, TMEM double buffering and epilogue as w4a4_gemm_persistent,
 // but the expansion warps read the packed int4 bytes straight from L2 with
-// 16-byte non-allocating loads, three K blocks ahead in registers, instead of
+// 16-byte non-allocating loads, two K blocks ahead in registers, instead of
 // staging them through shared memory with TMA. Shared memory then only holds
 // the expanded int8 stages (written once by the expansion warps, read once by
 // the tensor cores): half the shared-memory traffic per K block.
 //   warps 0-3 epilogue, warp 4 TMEM allocator + MMA issuer, warps 5-12 expansion.
 template <int BN>
 struct LCfg {
-  static constexpr int kThreads = 416;
+  static constexpr int kThreads = 544;  // 8 epilogue + 1 MMA + 8 expansion warps
   static constexpr int kRows = 128 + BN;
   static constexpr int kExpP = 128 * 128;
   static constexpr int kExpStage = kRows * 128;
-  static constexpr int ES = (192 * 1024) / kExpStage;
+  static constexpr int ES = (200 * 1024) / kExpStage;
   static constexpr int UPT = kRows * 4 / kExpandThreads;
-  static constexpr int D = 3;                      // K blocks in flight per expansion thread
+  static constexpr int D = 2;                      // K blocks in flight per expansion thread
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kBarBytes = (2 * ES + 5) * 8 + 16;
-  static constexpr int kSmemBytes = 1024 + ES * kExpStage + kBarBytes;
+  static constexpr int kEpiBytes = static_cast<int>(sizeof(EpiStage<BN>));
+  static constexpr int kSmemBytes = 1024 + ES * kExpStage + kBarBytes + kEpiBytes;
   static_assert(BN == 128 || BN == 256, "direct-load kernel uses N tiles of 128 or 256");
   static_assert(ES >= 2, "need two expanded stages");
   static_assert(kRows * 4 % kExpandThreads == 0, "expansion chunks must divide evenly");
@@ -916,7 +917,7 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
 }
 
 template <int BN>
-__global__ void __launch_bounds__(416, 1) w4a4_gemm_persistent_ldg(const GemmParams p) {
+__global__ void __launch_bounds__(544, 1) w4a4_gemm_persistent_ldg(const GemmParams p) {
   using C = LCfg<BN>;
   constexpr int ES = C::ES, UPT = C::UPT, D = C::D;
   extern __shared__ uint8_t smem_dyn[];
@@ -930,6 +931,7 @@ __global__ void __launch_bounds__(416, 1) w4a4_gemm_persistent_ldg(const GemmPar
   uint64_t* mma_done = tmem_full + 4;    // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  EpiStage<BN>* est = reinterpret_cast<EpiStage<BN>*>(reinterpret_cast<uint8_t*>(bars) + C::kBarBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = p.tiles_i * p.tiles_j;
@@ -942,13 +944,13 @@ __global__ void __launch_bounds__(416, 1) w4a4_gemm_persistent_ldg(const GemmPar
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 4);
+      mbar_init(&tmem_empty[a], kEpiWarps);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
@@ -957,7 +959,7 @@ __global__ void __launch_bounds__(416, 1) w4a4_gemm_persistent_ldg(const GemmPar
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_i8(128, BN);
@@ -987,9 +989,9 @@ __global__ void __launch_bounds__(416, 1) w4a4_gemm_persistent_ldg(const GemmPar
       }
       umma_commit(mma_done);
     }
-  } else if (warp >= 5) {
+  } else if (warp >= 9) {
     // ------------------------------------------------ load + expand (8 warps)
-    const int et = threadIdx.x - 5 * 32;
+    const int et = threadIdx.x - 9 * 32;
     const int my_tiles = (ntiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                          static_cast<int>(gridDim.x);
     const int total = my_tiles > 0 ? my_tiles * kb_n : 0;
@@ -1029,42 +1031,29 @@ __global__ void __launch_bounds__(416, 1) w4a4_gemm_persistent_ldg(const GemmPar
       if (lane == 0) mbar_arrive(&exp_full[es]);
       return true;
     };
-    uint4 w0[UPT], w1[UPT], w2[UPT];
-    static_assert(D == 3, "register ring is unrolled for three K blocks");
+    uint4 w0[UPT], w1[UPT];
+    static_assert(D == 2, "register ring is unrolled for two K blocks");
     load(0, w0);
     load(1, w1);
-    load(2, w2);
-    for (int g = 0; g < total; g += 3) {
+    for (int g = 0; g < total; g += 2) {
       if (!expand(g, w0)) break;
-      load(g + 3, w0);
+      load(g + 2, w0);
       if (g + 1 >= total) break;
       if (!expand(g + 1, w1)) break;
-      load(g + 4, w1);
-      if (g + 2 >= total) break;
-      if (!expand(g + 2, w2)) break;
-      load(g + 5, w2);
+      load(g + 3, w1);
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 0-3)
-    const int row_local = warp * 32 + lane;
+    // ------------------------------------------------ epilogue (warps 0-7)
     int t = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t) {
       const int acc_i = t & 1, use = t >> 1;
+      const int ti = tile % p.tiles_i, tj = tile / p.tiles_i;
+      epilogue_stage<BN>(p, tj, t & 1, est, threadIdx.x);
       bool ok = mbar_wait(&tmem_full[acc_i], use & 1u, abort_flag);
-      ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+      ok = named_bar_and(1, kEpiThreads, ok && !*abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const int ti = tile % p.tiles_i, tj = tile / p.tiles_i;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(acc_i * BN);
-      for (int j0 = 0; j0 < BN; j0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(t_row + j0, r);
-        tmem_ld_wait();
-        int32_t acc[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) acc[q] = static_cast<int32_t>(r[q]) >> 8;
-        epilogue16<BN, false>(p, ti, tj, row_local, j0, acc);
-      }
+      epilogue_tile<BN>(p, ti, tj, tmem_base + static_cast<uint32_t>(acc_i * BN), warp, lane, est, t & 1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[acc_i]);
@@ -1073,7 +1062,7 @@ __global__ void __launch_bounds__(416, 1) w4a4_gemm_persistent_ldg(const GemmPar
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) mbar_wait(mma_done, 0, nullptr);
     __syncwarp();
     tc_fence_after();
