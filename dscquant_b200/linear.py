@@ -109,6 +109,43 @@ class QuantLinear(nn.Module):
         self._prep = dict(packed=q.packed, sw=q.scales, wsum=q.row_sums, bias=bias, K=K, N=N, KP=KP,
                           aclip=float(self.activation_clip), bias_cache={})
 
+    # ------------------------------------------------------------------ packed-weight format
+    PREPARED_FORMAT = "dscq-w4a4-v1"
+
+    def prepared_state(self) -> dict:
+        """The prepared weight as plain tensors (CPU copies) plus the spec needed to use it:
+        packed int4 [N, KP/2] (the reference's packing), channel scales, code sums, bias, and the
+        quantisation / rotation settings. `load_prepared` restores it without re-quantising."""
+        if self._prep is None:
+            self.prepare()
+        p = self._prep
+        return {
+            "format": self.PREPARED_FORMAT,
+            "K": p["K"], "N": p["N"], "KP": p["KP"],
+            "weight_packed": p["packed"].cpu(), "weight_scales": p["sw"].cpu(), "weight_code_sums": p["wsum"].cpu(),
+            "bias": None if p["bias"] is None else p["bias"].detach().cpu(),
+            "activation_clip": p["aclip"], "weight_clip": float(self.weight_clip),
+            "activation_symmetric": self.symmetric, "online_rotation": self.rotate,
+        }
+
+    def load_prepared(self, state: dict) -> None:
+        """Installs a `prepared_state()` on this module's device (checks the format and shapes)."""
+        if state.get("format") != self.PREPARED_FORMAT:
+            raise ValueError(f"unknown prepared-weight format {state.get('format')!r}")
+        K, N = self.base.in_features, self.base.out_features
+        if (state["K"], state["N"]) != (K, N) or tuple(state["weight_packed"].shape) != (N, state["KP"] // 2):
+            raise ValueError("prepared weight does not match this layer's shape")
+        if bool(state["activation_symmetric"]) != self.symmetric or bool(state["online_rotation"]) != self.rotate:
+            raise ValueError("prepared weight was made for a different activation scheme / rotation setting")
+        dev = self.base.weight.device
+        bias = state["bias"]
+        self._prep = dict(packed=state["weight_packed"].to(dev), sw=state["weight_scales"].to(dev),
+                          wsum=state["weight_code_sums"].to(dev), bias=None if bias is None else bias.to(dev),
+                          K=K, N=N, KP=int(state["KP"]), aclip=float(state["activation_clip"]), bias_cache={})
+        with torch.no_grad():
+            self.weight_clip.fill_(float(state["weight_clip"]))
+            self.activation_clip.fill_(float(state["activation_clip"]))
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not self.enabled:
             return self.base(x)

@@ -103,3 +103,26 @@ def test_no_cpu_fallback():
                lambda: quantization.pack_int4(torch.zeros(2, 2, dtype=torch.int8))):
         with pytest.raises(RuntimeError):
             fn()
+
+
+def test_prepared_state_roundtrip_cpu():
+    """Packed-weight format: save/load of the prepared tensors and spec (no GPU work involved)."""
+    import torch
+    from torch import nn
+
+    from dscquant_b200 import QuantConfig, QuantLinear
+
+    base = nn.Linear(128, 8, bias=True, dtype=torch.bfloat16)
+    ql = QuantLinear(base, QuantConfig())
+    state = {"format": QuantLinear.PREPARED_FORMAT, "K": 128, "N": 8, "KP": 128,
+             "weight_packed": torch.zeros((8, 64), dtype=torch.uint8), "weight_scales": torch.ones(8),
+             "weight_code_sums": torch.zeros(8, dtype=torch.int32), "bias": torch.zeros(8, dtype=torch.bfloat16),
+             "activation_clip": 0.9, "weight_clip": 0.95, "activation_symmetric": True, "online_rotation": True}
+    ql.load_prepared(state)
+    assert ql._prep["KP"] == 128 and abs(float(ql.activation_clip) - 0.9) < 1e-6
+    with pytest.raises(ValueError):
+        ql.load_prepared(dict(state, format="other"))
+    with pytest.raises(ValueError):
+        ql.load_prepared(dict(state, online_rotation=False))
+    with pytest.raises(ValueError):
+        ql.load_prepared(dict(state, K=64))

@@ -136,3 +136,19 @@ def test_fp16_and_fp32_inputs(cuda_device):
         assert y.dtype == dt
         rel = (y.float() - base(x).float()).norm() / base(x).float().norm()
         assert rel < 0.25
+
+
+def test_prepared_state_roundtrip_gpu(cuda_device):
+    """A layer loaded from another layer's prepared state produces bit-identical outputs."""
+    from dscquant_b200 import QuantConfig, QuantLinear
+
+    K, N = 4096, 384
+    w = synthetic.weights_bf16(N, K, seed=9)
+    a = QuantLinear(_linear(w, None, cuda_device), QuantConfig())
+    a.enabled = True
+    st = a.prepared_state()
+    b = QuantLinear(nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=cuda_device), QuantConfig())
+    b.enabled = True
+    b.load_prepared(st)
+    x = torch.randn(33, K, device=cuda_device, dtype=torch.bfloat16)
+    assert torch.equal(a(x), b(x))
