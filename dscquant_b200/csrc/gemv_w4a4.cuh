@@ -65,14 +65,19 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4a4_gemv(const GemmParams p)
 #pragma unroll
     for (int i = 0; i < kGemvChunksPerWarp; ++i) {
       const int c = c_base + i;
+      // The skip must be warp-uniform: mma.sync needs all 32 lanes. In a
+      // ragged last chunk (kbytes % 64 == 32) lanes q = 2, 3 have no bytes;
+      // they feed zeros to the MMA instead of leaving it.
+      if (c >= kchunks) continue;
       const int off = c * 64 + q * 16;
-      if (c >= kchunks || off >= p.kbytes) continue;
+      const bool inK = off < p.kbytes;
       uint4 xv[NT];
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         const int m = t * 8 + g;
-        xv[t] = m < p.M ? __ldg(reinterpret_cast<const uint4*>(X + static_cast<int64_t>(m) * p.kbytes + off))
-                        : make_uint4(0, 0, 0, 0);
+        xv[t] = (inK && m < p.M)
+                    ? __ldg(reinterpret_cast<const uint4*>(X + static_cast<int64_t>(m) * p.kbytes + off))
+                    : make_uint4(0, 0, 0, 0);
       }
       const uint32_t wA[4] = {wa[i].x, wa[i].y, wa[i].z, wa[i].w};
       const uint32_t wB[4] = {wb[i].x, wb[i].y, wb[i].z, wb[i].w};
