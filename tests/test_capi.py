@@ -126,3 +126,10 @@ def test_prepared_state_roundtrip_cpu():
         ql.load_prepared(dict(state, online_rotation=False))
     with pytest.raises(ValueError):
         ql.load_prepared(dict(state, K=64))
+
+
+def test_host_pipeline_needs_cuda_device():
+    from dscquant_b200.hostio import HostPipeline
+
+    with pytest.raises(RuntimeError):
+        HostPipeline("cpu")

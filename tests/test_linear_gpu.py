@@ -152,3 +152,31 @@ def test_prepared_state_roundtrip_gpu(cuda_device):
     b.load_prepared(st)
     x = torch.randn(33, K, device=cuda_device, dtype=torch.bfloat16)
     assert torch.equal(a(x), b(x))
+
+
+def test_host_pipeline_matches_forward(cuda_device):
+    """HostPipeline (pinned host in/out, copies overlapped with the kernels on three streams) returns the
+    same bits as QuantLinear.forward on device tensors, over repeated calls that reuse its buffers."""
+    from dscquant_b200 import QuantConfig, QuantLinear
+    from dscquant_b200.hostio import HostPipeline
+
+    shapes = [(4096, 512), (4096, 1024), (11008, 256)]
+    mods, h_in, h_out, refs = [], [], [], []
+    for i, (K, N) in enumerate(shapes):
+        ql = QuantLinear(_linear(synthetic.weights_bf16(N, K, seed=40 + i), None, cuda_device), QuantConfig())
+        ql.enabled = True
+        x = torch.randn(96, K, device=cuda_device, dtype=torch.bfloat16)
+        refs.append(ql(x).cpu())
+        mods.append(ql)
+        h_in.append(x.cpu().pin_memory())
+        h_out.append(torch.empty((96, N), dtype=torch.bfloat16).pin_memory())
+    pipe = HostPipeline(cuda_device)
+    for _ in range(3):
+        for h in h_out:
+            h.zero_()
+        pipe.run(mods, h_in, h_out)
+        pipe.synchronize()
+        for h, r in zip(h_out, refs):
+            assert torch.equal(h, r)
+    with pytest.raises(ValueError):
+        pipe.run(mods, [t.clone() for t in h_in], h_out)  # not pinned
