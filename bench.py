@@ -59,10 +59,41 @@ def parse():
     p.add_argument("--N", type=int, default=11008)
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--variant", type=int, default=0, help="dscq_matmul variant for --kernel-case gemm")
+    p.add_argument("--qvariant", default="auto", choices=["auto", "tc", "legacy"],
+                   help="rotate+quantize kernel for --kernel-case quant")
     p.add_argument("--graph", action="store_true",
                    help="--kernel-case gemm: time REPS launches replayed from one CUDA graph (device time per launch, "
                         "no host launch overhead), cycling weight copies so the launches stream weights from HBM")
     return p.parse_args()
+
+
+def _graph_time(fn, R: int, dev) -> float:
+    """Median device time (ms) per call of fn(i), i = 0..R-1, replayed from one CUDA graph."""
+    import torch
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(R):
+            fn(i)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(R):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) / R)
+    del g
+    return statistics.median(ts)
 
 
 def kernel_case(args) -> None:
@@ -76,8 +107,19 @@ def kernel_case(args) -> None:
     bf = lambda b: torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16).to(dev)  # noqa: E731
     x = bf(synthetic.activations_bf16(args.M, args.K, seed=1))
     if args.kernel_case == "quant":
-        fn = lambda: ops.rowquant(x, "act_sym", rotate=True, KP=args.K)  # noqa: E731
         units = args.M * args.K * 2.5 + 4 * args.M
+        # input copies: enough that consecutive graph launches never find their rows in the 126 MB L2
+        copies = max(1, min(64, -(-(256 << 20) // (args.M * args.K * 2)))) if args.graph else 1
+        xs = [x] + [x.clone() for _ in range(copies - 1)]
+
+        def fn(i=0):
+            return ops.rowquant(xs[i % copies], "act_sym", rotate=True, KP=args.K, variant=args.qvariant)
+        if args.graph:
+            t = _graph_time(fn, max(args.reps, copies), dev)
+            print(json.dumps({"kernel_case": "quant", "qvariant": args.qvariant, "M": args.M, "K": args.K, "ms": t,
+                              "rate": units / (t * 1e-3) / 1e9, "unit": "GB/s", "graph_launches": max(args.reps, copies),
+                              "input_copies": copies}))
+            return
     else:
         w = bf(synthetic.weights_bf16(args.N, args.K, seed=2))
         qw = ops.rowquant(w, "weight_sym", rotate=True, KP=args.K)
@@ -99,33 +141,11 @@ def kernel_case(args) -> None:
         units = 2.0 * args.M * args.N * args.K
         if args.graph:
             R = max(args.reps, copies)
-            side = torch.cuda.Stream(dev)
-            side.wait_stream(torch.cuda.current_stream(dev))
-            with torch.cuda.stream(side):
-                for i in range(R):
-                    fn(i)
-            torch.cuda.current_stream(dev).wait_stream(side)
-            torch.cuda.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                for i in range(R):
-                    fn(i)
-            g.replay()
-            torch.cuda.synchronize()
-            ts = []
-            for _ in range(5):
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                g.replay()
-                e1.record()
-                torch.cuda.synchronize()
-                ts.append(e0.elapsed_time(e1) / R)
-            t = statistics.median(ts)
+            t = _graph_time(fn, R, dev)
             print(json.dumps({"kernel_case": "gemm", "variant": args.variant, "M": args.M, "K": args.K, "N": args.N,
                               "ms": t, "rate": units / (t * 1e-3) / 1e12, "unit": "TOPS", "graph_launches": R,
                               "weight_copies": copies,
                               "weight_GBps": wbytes / (t * 1e-3) / 1e9}))
-            del g
             return
     fn()
     torch.cuda.synchronize()
@@ -557,14 +577,12 @@ def main():
                "sample": f"{rows} tokens x 7 layer linears per step, {n} steps, oracle C W4A4 linear "
                          "(rotation, symmetric int4 codes, int32 GEMM, epilogue) with pthreads"}
 
+    # DRAM bytes per GEMM launch from one ncu capture of each benchmark shape at M = 2048
+    # (dram__bytes_read.sum + dram__bytes_write.sum), launch-weighted over the step's 7 GEMMs
     traffic = None
-    tpath = os.path.join(ROOT, "profiles", "gemm_dram_traffic.json")
-    if os.path.exists(tpath):
-        try:
-            with open(tpath) as f:
-                traffic = json.load(f).get("bytes_per_launch_at_bench_shape")
-        except Exception:
-            traffic = None
+    if M == 2048:
+        per_shape = {(4096, 4096): 12.662e6, (4096, 11008): 26.866e6, (11008, 4096): 33.891e6}
+        traffic = sum(per_shape[(k, n)] for _, k, n in LAYER) / len(LAYER)
 
     if rank == 0:
         line = {
@@ -578,8 +596,9 @@ def main():
                        "parallelism": f"dp{world} over tokens" if world > 1 else "single GPU",
                        "l2": f"{R} layer replicas cycled (working set > 126 MB L2)"},
             "gpu_launches": 11 * args.steps,
-            "roofline": {"kernel": "w4a4_gemm_tc", "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
+            "roofline": {"kernel": "w4a4_gemm_persistent", "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
                          "unit": "TFLOP/s", "frac": gemm_tops / int8_peak, "traffic": traffic,
+                         "traffic_note": "bytes per launch, ncu capture at M=2048 (profiles/)",
                          "peak_note": f"int8 dense = 2 x {peaks['source']} bf16 cuBLAS {peaks['bf16_tflops']} TFLOP/s; "
                                       "ops are integer ops (2 per MAC)",
                          "share_of_step": gemm_ms / elapsed_ms},

@@ -17,6 +17,7 @@ DSCQ_OK, DSCQ_ERR_INVALID, DSCQ_ERR_CUDA, DSCQ_ERR_UNSUPPORTED, DSCQ_ERR_RANGE =
 BF16, F16, F32 = 0, 1, 2
 ACT_SYM, WEIGHT_SYM, ACT_ASYM, ACT_ASYM_TORCH = 0, 1, 2, 3
 GEMM_AUTO, GEMM_SMALL_M, GEMM_LARGE_M, GEMM_LARGE_M_DIRECT, GEMM_LARGE_M_PAIR, GEMM_SMALL_M_TC = 0, 1, 2, 3, 4, 5
+QUANT_AUTO, QUANT_TC, QUANT_LEGACY = 0, 1, 2
 
 _i32, _i64, _u32p, _f32, _vp, _cp = (ctypes.c_int, ctypes.c_int64, ctypes.POINTER(ctypes.c_uint32), ctypes.c_float,
                                      ctypes.c_void_p, ctypes.c_char_p)
@@ -31,6 +32,8 @@ SIGNATURES = {
     "dscq_quantize": (_i32, [_vp, _i32, _i64, _i64, _f32, _i32, _vp, _vp, _vp, _vp]),
     "dscq_rowquant": (_i32, [_vp, _i32, _i64, _i64, _i64, _i32, _i32, _vp, _i32, _f32, _i64, _i64, _vp, _i64, _vp,
                              _vp, _vp, _vp, _i64, _vp]),
+    "dscq_rowquant_variant": (_i32, [_vp, _i32, _i64, _i64, _i64, _i32, _i32, _vp, _i32, _f32, _i64, _i64, _vp,
+                                     _i64, _vp, _vp, _vp, _vp, _i64, _i32, _vp]),
     "dscq_matmul": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i32, _vp]),
     "dscq_matmul_cols": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32,
                                 ctypes.POINTER(ctypes.c_void_p), _i32, _i64, _i64, _i32, _vp]),

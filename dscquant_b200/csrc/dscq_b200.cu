@@ -17,6 +17,7 @@
 #include "wht_quant.cuh"
 #include "kron_quant.cuh"
 #include "gemv_w4a4.cuh"
+#include "rotq_tc.cuh"
 
 namespace {
 
@@ -94,6 +95,22 @@ int make_u8_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, 
   return DSCQ_OK;
 }
 
+// x [M, ld_x] bf16 viewed as a 3-D tensor {c: 64, i: ap, token: M} (row k = i*64 + c), boxes of
+// {64, ap16, P} landing in shared memory with the 128-byte swizzle (the MN-major UMMA layout).
+int make_rows_map(CUtensorMap* map, const void* x, int64_t M, int ap, int64_t ld_x, int ap16, int P) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {64u, static_cast<cuuint64_t>(ap), static_cast<cuuint64_t>(M)};
+  cuuint64_t strides[2] = {128u, static_cast<cuuint64_t>(ld_x) * 2u};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(ap16), static_cast<cuuint32_t>(P)};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(x), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled (rows) failed (" + std::to_string(r) + ")");
+  return DSCQ_OK;
+}
+
 int g_num_sms = 0;
 
 int num_sms() {
@@ -150,6 +167,22 @@ cudaError_t launch_kron(const dscq::RowQuantParams& p, int a, int s, cudaStream_
   if (e != cudaSuccess) return e;
   const int grid = std::min(p.rows_out, num_sms());
   dscq::kron_quant<AP><<<grid, C::THREADS, C::SMEM, st>>>(p, a, s);
+  return cudaGetLastError();
+}
+
+template <int MT>
+cudaError_t launch_rotq(const CUtensorMap& tm, const dscq::RotqParams& rp, cudaStream_t st) {
+  // at least 120 KB so that one CTA (which allocates all 512 TMEM columns) occupies an SM
+  const size_t smem = std::max<size_t>(1024 + rp.a_bytes + static_cast<size_t>(rp.ns) * rp.stage_bytes + 1024,
+                                       120 * 1024);
+  cudaError_t e = cudaFuncSetAttribute(dscq::rotq_tc<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const int grid = std::min(rp.groups, num_sms());
+  const int nwarps = std::max(rp.tma_warp, rp.mma_warp) + 1;
+  const int threads = std::max(nwarps, (rp.nteam - 1) * rp.team_stride + rp.tw) * 32;
+  if (threads > dscq::kRqMaxThreads) return cudaErrorInvalidConfiguration;
+  dscq::rotq_tc<MT><<<grid, threads, smem, st>>>(tm, rp);
   return cudaGetLastError();
 }
 
@@ -276,6 +309,15 @@ int dscq_rowquant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x
                   const int8_t* h_a, int mode, float clip, int64_t rows_out, int64_t KP, uint8_t* packed,
                   int64_t ld_packed, float* scales, int32_t* zeros, int32_t* row_sums, int8_t* codes,
                   int64_t ld_codes, void* stream) {
+  return dscq_rowquant_variant(x, x_dtype, M, K, ld_x, rotate, rot_a, h_a, mode, clip, rows_out, KP, packed, ld_packed,
+                               scales, zeros, row_sums, codes, ld_codes, DSCQ_QUANT_AUTO, stream);
+}
+
+int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x, int rotate, int rot_a,
+                          const int8_t* h_a, int mode, float clip, int64_t rows_out, int64_t KP, uint8_t* packed,
+                          int64_t ld_packed, float* scales, int32_t* zeros, int32_t* row_sums, int8_t* codes,
+                          int64_t ld_codes, int variant, void* stream) {
+  DSCQ_REQUIRE(variant >= DSCQ_QUANT_AUTO && variant <= DSCQ_QUANT_LEGACY, "unknown quantizer variant");
   DSCQ_REQUIRE(x && packed && scales, "x, packed and scales must not be null");
   DSCQ_REQUIRE(x_dtype == DSCQ_BF16 || x_dtype == DSCQ_F16 || x_dtype == DSCQ_F32, "x_dtype must be bf16/f16/f32");
   DSCQ_REQUIRE(M >= 1 && M <= (1 << 24), "require 1 <= M <= 2^24");
@@ -323,6 +365,53 @@ int dscq_rowquant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x
   p.ld_codes = ld_codes;
 
   cudaStream_t cst = static_cast<cudaStream_t>(stream);
+  // tcgen05 path: K = a' * 64, a' <= 256, symmetric modes, bf16 rows, 16-byte aligned outputs
+  const bool sym = mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM;
+  const int ap_tc = (rotate && log2b >= 6) ? static_cast<int>(K / 64) : 0;
+  const bool tc_ok = rotate && log2b >= 6 && ap_tc >= 16 && ap_tc <= 256 && sym && x_dtype == DSCQ_BF16 &&
+                     KP == K && aligned(x, 16) && ld_x % 8 == 0 && aligned(packed, 16) && ld_packed % 16 == 0 &&
+                     (!codes || (aligned(codes, 16) && ld_codes % 16 == 0));
+  if (variant == DSCQ_QUANT_TC && !tc_ok)
+    return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize needs a rotation with K = a' * 64 (a' <= 256), a "
+                                      "symmetric mode, bf16 input, KP == K and 16-byte aligned rows");
+  if (tc_ok && (variant == DSCQ_QUANT_TC || (variant == DSCQ_QUANT_AUTO && ap_tc >= 32))) {
+    dscq::RotqParams rp;
+    rp.p = p;
+    rp.a_base = p.rot_a;
+    rp.s_log = log2b - 6;
+    rp.ap = ap_tc;
+    rp.ap16 = (ap_tc + 15) / 16 * 16;
+    rp.P = (rp.ap16 == 32 || rp.ap16 == 64) ? 128 / rp.ap16 : 1;
+    rp.log2_ap16 = rp.ap16 == 32 ? 5 : 6;
+    rp.mt = rp.ap16 <= 128 ? 1 : 2;
+    rp.groups = static_cast<int>((rows_out + rp.P - 1) / rp.P);
+    rp.ksteps = (rp.mt == 1 ? rp.P * rp.ap16 : rp.ap16) / 16;
+    rp.nkb = (rp.ksteps * 16 + 63) / 64;
+    rp.a_bytes = static_cast<uint32_t>(rp.mt * rp.nkb * 16384);
+    rp.stage_bytes = static_cast<uint32_t>(rp.P * rp.ap16 * 128);
+    rp.ns = std::min<int>(dscq::kRqMaxStages, (210 * 1024 - static_cast<int>(rp.a_bytes)) / static_cast<int>(rp.stage_bytes));
+    if (rp.mt == 1) {  // three teams of four warps (lane quadrants 0-3), then the TMA and MMA warps
+      rp.tw = 4;
+      rp.team_stride = 4;
+      rp.nteam = 3;
+      rp.tma_warp = 12;
+      rp.mma_warp = 13;
+    } else {  // two teams of 4 + ceil((a' - 128) / 32) warps at warps 0.. and 8..
+      rp.tw = 4 + (rp.ap - 128 + 31) / 32;
+      rp.team_stride = 8;
+      rp.nteam = 2;
+      rp.tma_warp = rp.tw <= 6 ? 6 : (rp.tw == 7 ? 7 : 16);
+      rp.mma_warp = rp.tw <= 6 ? 7 : (rp.tw == 7 ? 15 : 17);
+    }
+    if (rp.ns < 2 || static_cast<int64_t>(rp.a_base) * rp.a_base > static_cast<int64_t>(rp.ns) * rp.stage_bytes)
+      return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize: shared memory too small");
+    CUtensorMap tm;
+    st = make_rows_map(&tm, x, M, rp.ap, ld_x, rp.ap16, rp.P);
+    if (st) return st;
+    cudaError_t e = rp.mt == 1 ? launch_rotq<1>(tm, rp, cst) : launch_rotq<2>(tm, rp, cst);
+    if (e != cudaSuccess) return cuda_fail(e, "launch rotq_tc");
+    return DSCQ_OK;
+  }
   const bool fast = rotate && p.rot_a == 1 && log2b >= 10 && log2b <= 13 &&
                     (mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM) && x_dtype == DSCQ_BF16 && KP == K &&
                     aligned(x, 16) && ld_x % 8 == 0 && aligned(packed, 2) && ld_packed % 2 == 0;

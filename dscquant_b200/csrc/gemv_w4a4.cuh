@@ -3,9 +3,10 @@
 //
 // Each CTA owns 16 weight rows (output channels) and splits K across its 8
 // warps. A warp streams its weight rows straight from HBM into registers with
-// 16-byte loads (all of them issued before the first MMA), expands the
-// nibbles in registers (byte = nibble << 4, int8 value 16*code, as in the
-// tcgen05 kernels) and issues legacy mma.sync.m16n8k32 int8 MMAs: A = 16
+// 16-byte loads (a pass's weight and activation loads all issued before its
+// first MMA), expands the nibbles in registers (byte = nibble << 4, int8
+// value 16*code, as in the tcgen05 kernels) and issues legacy
+// mma.sync.m16n8k32 int8 MMAs: A = 16
 // weight rows x 32 k, B = 32 k x 8 tokens, int32 accumulators. Any k order
 // shared by both operands gives the same dot product, so thread q of a quad
 // takes bytes [16q, 16q+16) of every 64-byte (128-element) row chunk and uses
@@ -33,9 +34,11 @@ __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
 }
 
 constexpr int kGemvWarps = 8;
-constexpr int kGemvChunksPerWarp = 8;  // 128-element K chunks held in registers per warp and pass
+constexpr int kGemvChunksPerWarp = 4;  // 128-element K chunks per warp and pass, loaded up front
 
-// NT = number of 8-token MMA column tiles (M <= 8 * NT).
+// NT = number of 8-token MMA column tiles (M <= 8 * NT). Pass p of warp w covers the K chunks
+// c = (p * 8 + w) * 4 + i, i < 4: all eight warps share every pass, and each pass issues the
+// weight AND activation loads of its four chunks before the first MMA.
 template <int NT>
 __global__ void __launch_bounds__(kGemvWarps * 32) w4a4_gemv(const GemmParams p) {
   __shared__ int red[kGemvWarps][16][8 * NT];
@@ -52,33 +55,28 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4a4_gemv(const GemmParams p)
 
   const int rA = n0 + g, rB = n0 + g + 8;
   const bool okA = rA < p.N, okB = rB < p.N;
-  for (int c_base = warp * kGemvChunksPerWarp; c_base < kchunks; c_base += kGemvWarps * kGemvChunksPerWarp) {
-    uint4 wa[kGemvChunksPerWarp], wb[kGemvChunksPerWarp];
+  constexpr int CPW = kGemvChunksPerWarp;
+  for (int c_base = warp * CPW; c_base < kchunks; c_base += kGemvWarps * CPW) {
+    uint4 wa[CPW], wb[CPW], xv[CPW][NT];
 #pragma unroll
-    for (int i = 0; i < kGemvChunksPerWarp; ++i) {
+    for (int i = 0; i < CPW; ++i) {
       const int c = c_base + i;
       const int off = c * 64 + q * 16;
       const bool inK = c < kchunks && off < p.kbytes;
       wa[i] = (inK && okA) ? ldg_stream_v4(W + static_cast<int64_t>(rA) * p.kbytes + off) : make_uint4(0, 0, 0, 0);
       wb[i] = (inK && okB) ? ldg_stream_v4(W + static_cast<int64_t>(rB) * p.kbytes + off) : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int i = 0; i < kGemvChunksPerWarp; ++i) {
-      const int c = c_base + i;
-      // The skip must be warp-uniform: mma.sync needs all 32 lanes. In a
-      // ragged last chunk (kbytes % 64 == 32) lanes q = 2, 3 have no bytes;
-      // they feed zeros to the MMA instead of leaving it.
-      if (c >= kchunks) continue;
-      const int off = c * 64 + q * 16;
-      const bool inK = off < p.kbytes;
-      uint4 xv[NT];
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         const int m = t * 8 + g;
-        xv[t] = (inK && m < p.M)
-                    ? __ldg(reinterpret_cast<const uint4*>(X + static_cast<int64_t>(m) * p.kbytes + off))
-                    : make_uint4(0, 0, 0, 0);
+        xv[i][t] = (inK && m < p.M)
+                       ? __ldg(reinterpret_cast<const uint4*>(X + static_cast<int64_t>(m) * p.kbytes + off))
+                       : make_uint4(0, 0, 0, 0);
       }
+    }
+#pragma unroll
+    for (int i = 0; i < CPW; ++i) {
+      // Lanes without bytes in a ragged last chunk hold zeros; every lane runs every mma.sync.
+      if (c_base + i >= kchunks) continue;  // warp-uniform
       const uint32_t wA[4] = {wa[i].x, wa[i].y, wa[i].z, wa[i].w};
       const uint32_t wB[4] = {wb[i].x, wb[i].y, wb[i].z, wb[i].w};
 #pragma unroll
@@ -87,7 +85,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4a4_gemv(const GemmParams p)
         const uint32_t a[4] = {(wA[j] << 4) & MSK, (wB[j] << 4) & MSK, wA[j] & MSK, wB[j] & MSK};
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-          const uint32_t xw = j == 0 ? xv[t].x : (j == 1 ? xv[t].y : (j == 2 ? xv[t].z : xv[t].w));
+          const uint32_t xw = j == 0 ? xv[i][t].x : (j == 1 ? xv[i][t].y : (j == 2 ? xv[i][t].z : xv[i][t].w));
           mma_s8_16832(acc[t], a, (xw << 4) & MSK, xw & MSK);
         }
       }

@@ -209,6 +209,48 @@ __host__ __device__ constexpr uint32_t umma_idesc_i8(int m, int n) {
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 x bf16 -> f32 (kind::f16), one elected thread issues.
+__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// UMMA descriptor for an MN-major operand in the canonical 128-byte-swizzled
+// layout: each row of 128 bytes holds 64 consecutive MN elements (16-bit) of
+// one k, 8 consecutive k rows form a 1024-byte swizzle atom. Used with an MN
+// extent of exactly one atom (64 elements), so only the stride between 8-row
+// k groups matters; both offset fields carry it (1024 B).
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1024u >> 4) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16 with bf16 A and B, f32 D; A K-major,
+// B MN-major (bit 16), N>>3 at [17,23), M>>4 at [24,29).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// 3-D tiled bulk-tensor load global -> shared (x innermost, in elements).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05, CTA pairs
 // cta_group::2: one MMA spans the two CTAs of a cluster pair. Allocation and
 // release are executed by the same warp in both CTAs.

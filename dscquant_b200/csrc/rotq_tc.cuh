@@ -1,0 +1,416 @@
+// Fused Hadamard rotation + symmetric per-row int4 quantisation on the
+// tcgen05 tensor cores, for K = a' * 64 (a' <= 256) and bf16 input:
+//
+//   y = x (H' (x) H_64) / sqrt(K),  H' = H_a (x) H_(2^s) of order a',  k = i*64 + c
+//
+// (K = 4096: H' = H_64; K = 8192: H_128; K = 11008: the order-172 matrix;
+// K = 14336: H_28 (x) H_8). Per token the row is the matrix X [a'][64]; the
+// dense factor is one small GEMM D = H'^T X on the tensor cores, the 64-point
+// Walsh-Hadamard transform along c then runs in registers.
+//
+//   * TMA (3-D map {c, i, token}, 128-byte swizzle) lands one token group's
+//     X in shared memory as [token][i][64 c]: a k-by-MN operand whose 128-byte
+//     rows hold 64 consecutive c of one i, i.e. the canonical MN-major layout,
+//     consumed by tcgen05.mma kind::f16 without any rearrangement;
+//   * H'^T (A operand, K-major, 128 rows per M tile) is built once per CTA in
+//     shared memory. For a' <= 64 (a' = 32, 64) P = 128 / a' tokens share one
+//     MMA through a block-diagonal A (k = token*a' + i), so all 128 TMEM lanes
+//     carry data; a' in (128, 256] uses two M tiles;
+//   * D (f32, 128 lanes x 64 columns per M tile) accumulates in TMEM, up to
+//     8 token groups in flight (512 columns);
+//   * epilogue: each thread owns one TMEM lane (one i' of one token) and its
+//     64 columns: tcgen05.ld, 64-point WHT in registers (packed f32x2 adds),
+//     row absmax over the token's lanes (shuffles + shared memory), codes by
+//     the 1.5*2^23 round-half-even add, 32 contiguous packed bytes per thread.
+//
+// Warp roles (one CTA per SM, persistent over token groups): epilogue teams
+// take token groups round-robin. A team has one warp per 32-lane block of D:
+// four for M tile 0 (TMEM lane quadrants 0-3) plus, for two M tiles, one per
+// quadrant holding rows of M tile 1, so every thread handles exactly one row
+// of 64 values. One warp issues TMA, one owns TMEM and issues the MMAs. All
+// waits are bounded.
+#pragma once
+#include "ptx.cuh"
+#include "rowquant.cuh"
+
+namespace dscq {
+
+constexpr int kRqMaxThreads = 576;
+constexpr int kRqTmemCols = 512;
+constexpr int kRqMaxStages = 12;
+constexpr int kRqMaxTeams = 4;
+
+struct RotqParams {
+  RowQuantParams p;
+  int a_base, s_log;     // H' = H_a (x) H_(2^s)
+  int ap;                // a' = a_base << s_log
+  int ap16;              // a' rounded up to 16: k rows of one token in the B tile
+  int P;                 // tokens per MMA group (block-diagonal A when > 1)
+  int mt;                // M tiles (1 or 2)
+  int groups;            // ceil(rows_out / P)
+  int ns;                // B stages in shared memory
+  int ksteps;            // k steps of 16 per M tile
+  int nkb;               // 64-wide k atoms of A per M tile
+  uint32_t a_bytes;      // bytes of the A region (mt * nkb * 16 KB)
+  uint32_t stage_bytes;  // P * ap16 * 128
+  int log2_ap16;         // log2(ap16) when P > 1
+  int nteam;             // epilogue teams
+  int tw;                // warps per team
+  int team_stride;       // team t owns warps [t * team_stride, t * team_stride + tw)
+  int tma_warp, mma_warp;
+};
+
+// 64 consecutive TMEM columns of this thread's lane as 32 float2 (natural column order).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float2 (&u)[32]) {
+  uint32_t r0[32], r1[32];
+  tmem_ld32(taddr, r0);
+  tmem_ld32(taddr + 32u, r1);
+  tmem_ld_wait();
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    u[i] = make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+    u[16 + i] = make_float2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+  }
+}
+
+// In-place 64-point Walsh-Hadamard transform (Sylvester order, natural index) on u[i] = (v[2i], v[2i+1]):
+// one scalar stage inside each pair, five packed f32x2 stages between pairs.
+__device__ __forceinline__ void wht64_regs(float2 (&u)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) u[i] = make_float2(u[i].x + u[i].y, u[i].x - u[i].y);
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1)
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (!(i & h)) {
+        const float2 a = u[i], b = u[i + h];
+        u[i] = __fadd2_rn(a, b);
+        u[i + h] = __ffma2_rn(b, make_float2(-1.f, -1.f), a);
+      }
+}
+
+__device__ __forceinline__ float absmax64(const float2 (&u)[32]) {
+  float m0 = 0.f, m1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    m0 = fmaxf(m0, fabsf(u[i].x));
+    m1 = fmaxf(m1, fabsf(u[i].y));
+  }
+  return fmaxf(m0, m1);
+}
+
+__device__ __forceinline__ uint32_t bfi4(uint32_t src, uint32_t base, uint32_t pos) {
+  uint32_t d;
+  asm("bfi.b32 %0, %1, %2, %3, 4;" : "=r"(d) : "r"(src), "r"(base), "r"(pos));
+  return d;
+}
+
+// Codes of 64 values -> 32 packed bytes (even k in the low nibble) at prow;
+// optional int8 codes at crow; returns the code sum when SUMS.
+template <bool SUMS, bool CLAMP>
+__device__ __forceinline__ int quant_store64(const float2 (&u)[32], float cm, float lo, uint8_t* prow, int8_t* crow) {
+  uint32_t w[8];
+  int csum = 0;
+  const float2 cm2 = make_float2(cm, cm), magic = make_float2(12582912.f, 12582912.f);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      float2 q = __fmul2_rn(u[4 * j + t], cm2);
+      if (CLAMP) {
+        q.x = fminf(fmaxf(q.x, lo), 7.f);
+        q.y = fminf(fmaxf(q.y, lo), 7.f);
+      }
+      const float2 r = __fadd2_rn(q, magic);  // round half to even into the low mantissa bits
+      const uint32_t u0 = __float_as_uint(r.x), u1 = __float_as_uint(r.y);
+      word = bfi4(u0, word, 8 * t);
+      word = bfi4(u1, word, 8 * t + 4);
+      if (SUMS) csum += (static_cast<int>(u0 << 28) >> 28) + (static_cast<int>(u1 << 28) >> 28);
+    }
+    w[j] = word;
+  }
+  uint4* dst = reinterpret_cast<uint4*>(prow);
+  dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  if (crow) {
+    uint32_t cw[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      uint32_t x = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int c = 4 * j + t;
+        const uint32_t nib = (w[c >> 3] >> (4 * (c & 7))) & 15u;
+        x |= (static_cast<uint32_t>(static_cast<int>(nib << 28) >> 28) & 0xFFu) << (8 * t);
+      }
+      cw[j] = x;
+    }
+    uint4* cd = reinterpret_cast<uint4*>(crow);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) cd[j] = make_uint4(cw[4 * j], cw[4 * j + 1], cw[4 * j + 2], cw[4 * j + 3]);
+  }
+  return csum;
+}
+
+template <bool CLAMP>
+__device__ __forceinline__ int quant_row64(const float2 (&u)[32], float cm, float lo, bool sums, uint8_t* prow,
+                                           int8_t* crow) {
+  return sums ? quant_store64<true, CLAMP>(u, cm, lo, prow, crow) : quant_store64<false, CLAMP>(u, cm, lo, prow, crow);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kRqMaxThreads, 1)
+    rotq_tc(const __grid_constant__ CUtensorMap tmX, const RotqParams rp) {
+  const RowQuantParams& p = rp.p;
+  extern __shared__ uint8_t rq_smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rq_smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* a_base = smem;
+  uint8_t* b_base = smem + rp.a_bytes;
+  constexpr int S = kRqTmemCols / (MT * 64);  // TMEM slots (token groups in flight)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + rp.ns * rp.stage_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kRqMaxStages;
+  uint64_t* tfull = bars + 2 * kRqMaxStages;
+  uint64_t* tempty = tfull + S;
+  uint64_t* done = tempty + S;
+  uint64_t* aready = done + 1;  // A built, staging stage free
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aready + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red_max = reinterpret_cast<float*>(tmem_slot + 4);        // [team][parity][8]
+  int* red_sum = reinterpret_cast<int*>(red_max + kRqMaxTeams * 16);  // [team][parity][8]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ap = rp.ap, ap16 = rp.ap16, P = rp.P, ns = rp.ns, tw = rp.tw;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&tfull[s], 1);
+      mbar_init(&tempty[s], tw);
+    }
+    mbar_init(done, 1);
+    mbar_init(aready, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == rp.tma_warp && lane == 0) tma_prefetch_desc(&tmX);
+  if (warp == rp.mma_warp) {
+    tmem_alloc(tmem_slot, kRqTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int groups = rp.groups;
+  const int team = warp / rp.team_stride, idx = warp % rp.team_stride;
+  // Every warp except the TMA and MMA warps builds A while the first loads are in flight; the
+  // last B stages double as staging space for H_a and are loaded only once A is complete.
+  const bool builder = warp != rp.tma_warp && warp != rp.mma_warp;
+  const int nb = static_cast<int>(blockDim.x) - 64;
+  const int bt = static_cast<int>(threadIdx.x) - 32 * ((rp.tma_warp < warp) + (rp.mma_warp < warp));
+  const int h_stages = rp.a_base > 1 ? (rp.a_base * rp.a_base + static_cast<int>(rp.stage_bytes) - 1) /
+                                           static_cast<int>(rp.stage_bytes)
+                                     : 0;
+  const int stage_first = ns - h_stages;  // stages holding H_a until A is built
+  uint8_t* stage_h = b_base + stage_first * rp.stage_bytes;
+  if (builder) {
+    // ---- H_a^T staged in shared memory: ht[c * a + r] = H_a[r][c], so 8 consecutive k of one
+    // A row are 8 consecutive bytes.
+    const int8_t* ht = nullptr;
+    if (rp.a_base > 1) {
+      const int a = rp.a_base;
+      for (int i = bt; i < a * a; i += nb) {
+        const int r = i / a, c = i - r * a;
+        stage_h[c * a + r] = static_cast<uint8_t>(p.h_a[i]);
+      }
+      ht = reinterpret_cast<const int8_t*>(stage_h);
+    }
+    named_bar_sync(5, nb);
+    // ---- A = H'^T (K-major, 128-byte swizzle). Chunk u = (row << 5) | (kb << 3) | ch holds
+    // A[row][k0 .. k0+7], k0 = kb * 64 + ch * 8, row = m * 128 + r; A[i'][i] = H'[i][i'].
+    {
+      const int chunks = MT * 128 * 32;
+      const int s = rp.s_log, a = rp.a_base, msk = (1 << s) - 1;
+      for (int u = bt; u < chunks; u += nb) {
+        const int ch = u & 7, kb = (u >> 3) & 3, row = u >> 5;
+        if (kb >= rp.nkb) continue;
+        const int k0 = kb * 64 + ch * 8;
+        int ip, ikb;  // i' of the row and i of k0 inside the token block
+        bool row_live;
+        uint32_t klive = 0xFFu;  // live k of the chunk (bit j: k0 + j)
+        if (MT == 1 && P > 1) {
+          const int sh = rp.log2_ap16;
+          ip = row & (ap16 - 1);
+          ikb = k0 & (ap16 - 1);
+          row_live = ip < ap && (row >> sh) == (k0 >> sh);
+        } else {
+          ip = row;
+          ikb = k0;
+          row_live = ip < ap;
+        }
+        for (int j = 0; j < 8; ++j)
+          if (ikb + j >= ap) klive &= ~(1u << j);
+        uint32_t neg = 0;  // bit j: H'[ikb + j][ip] < 0
+        if (row_live && klive) {
+          for (int j = 0; j < 8; ++j) neg |= static_cast<uint32_t>(__popc((ikb + j) & ip & msk) & 1) << j;
+          if (a > 1) {
+            for (int j = 0; j < 8; ++j)
+              if (ikb + j < ap) neg ^= static_cast<uint32_t>(ht[(ip >> s) * a + ((ikb + j) >> s)] < 0) << j;
+          }
+        }
+        if (!row_live) klive = 0;
+        uint32_t wv[4];
+  #pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t lo = ((klive >> (2 * t)) & 1u) ? (0x3F80u | (((neg >> (2 * t)) & 1u) << 15)) : 0u;
+          const uint32_t hi = ((klive >> (2 * t + 1)) & 1u) ? (0x3F80u | (((neg >> (2 * t + 1)) & 1u) << 15)) : 0u;
+          wv[t] = lo | (hi << 16);
+        }
+        const int m = row >> 7, r = row & 127;
+        uint8_t* dst = a_base + (m * rp.nkb + kb) * 16384 + r * 128 + ((ch ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      }
+    }
+    fence_proxy_async_smem();  // A writes and the staging reads ordered before the async proxy
+    named_bar_sync(5, nb);
+    if (bt == 0) mbar_arrive(aready);
+  }
+
+  if (warp == rp.tma_warp) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int n = 0;
+      bool ok = true;
+      for (int g = blockIdx.x; g < groups; g += gridDim.x, ++n) {
+        const int s = n % ns;
+        if ((n >= stage_first && n < ns && !mbar_wait(aready, 0, abort_flag)) ||
+            (n >= ns && !mbar_wait(&empty[s], ((n / ns) & 1u) ^ 1u, abort_flag))) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], rp.stage_bytes);
+        tma_load_3d(b_base + s * rp.stage_bytes, &tmX, &full[s], 0, 0, g * P);
+      }
+      if (!ok) {  // let the loads already issued land before the CTA can exit
+        for (int j = n > ns ? n - ns : 0; j < n; ++j) mbar_wait(&full[j % ns], (j / ns) & 1u, nullptr);
+      }
+    }
+  } else if (warp == rp.mma_warp) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16_bmn(128, 64);
+      const uint32_t a0 = smem_u32(a_base);
+      int n = 0;
+      const bool a_ok = mbar_wait(aready, 0, abort_flag);
+      for (int g = blockIdx.x; a_ok && g < groups; g += gridDim.x, ++n) {
+        const int s = n % ns, slot = n % S, use = n / S;
+        if (use > 0 && !mbar_wait(&tempty[slot], (use - 1) & 1u, abort_flag)) break;
+        if (!mbar_wait(&full[s], (n / ns) & 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t b0 = smem_u32(b_base + s * rp.stage_bytes);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          const uint32_t d = tmem_base + static_cast<uint32_t>(slot * MT * 64 + m * 64);
+          for (int ks = 0; ks < rp.ksteps; ++ks) {
+            const uint64_t ad = umma_desc_sw128(a0 + (m * rp.nkb + (ks >> 2)) * 16384 + (ks & 3) * 32);
+            const uint64_t bd = umma_desc_sw128_mn(b0 + ks * 2048);
+            umma_f16_ss(d, ad, bd, idesc, ks > 0 ? 1u : 0u);
+          }
+        }
+        umma_commit(&empty[s]);
+        umma_commit(&tfull[slot]);
+      }
+      umma_commit(done);
+    }
+  } else if (team < rp.nteam && idx < tw) {
+    // ------------------------------------------------ epilogue team member: one 32-lane block of D
+    const int mtile = idx >> 2, qd = idx & 3;  // idx 0-3: M tile 0, idx 4..: M tile 1
+    const int r = qd * 32 + lane;              // TMEM lane = row of the M tile
+    const float lo = p.mode == kWeightSym ? -7.f : -8.f;
+    const bool clamp = p.clip < 1.f;
+    int ip, pr;  // i' of this thread's row, token inside the group
+    bool live;
+    if (MT == 1) {
+      pr = r / ap16;
+      ip = r % ap16;
+      live = pr < P && ip < ap;
+    } else {
+      pr = 0;
+      ip = mtile * 128 + r;
+      live = ip < ap;
+    }
+    const int wtok = P > 1 ? (qd * 32) / ap16 : 0;  // lanes of a warp never straddle two tokens
+    const int wpt = P > 1 ? ap16 / 32 : tw;        // team warps per token
+    const int first_w = wtok * wpt;
+    const int bar_id = 1 + team;
+    const int bar_cnt = tw * 32;
+    float* rmax = red_max + team * 16;
+    int* rsum = red_sum + team * 16;
+    int n = team, it = 0;
+    for (int g = blockIdx.x + team * gridDim.x; g < groups; g += rp.nteam * gridDim.x, n += rp.nteam, ++it) {
+      const int slot = n % S, use = n / S, par = it & 1;
+      bool ok = mbar_wait(&tfull[slot], use & 1u, abort_flag);
+      ok = named_bar_and(bar_id, bar_cnt, ok && !*abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      float2 v[32];
+      tmem_ld64(tmem_base + (static_cast<uint32_t>(qd * 32) << 16) + static_cast<uint32_t>(slot * MT * 64 + mtile * 64),
+                v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[slot]);  // this slot's columns may be overwritten
+
+      wht64_regs(v);
+      float amax = live ? absmax64(v) : 0.f;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0) rmax[par * 8 + idx] = amax;
+      named_bar_sync(bar_id, bar_cnt);
+      amax = 0.f;
+      for (int w = 0; w < wpt; ++w) amax = fmaxf(amax, rmax[par * 8 + first_w + w]);
+
+      const int token = g * P + (MT == 1 ? pr : 0);
+      const int wtoken = g * P + wtok;
+      const float amax_y = __fmul_rn(amax, p.norm);
+      const float scale = fmaxf(__fdiv_rn(__fmul_rn(amax_y, p.clip), 7.f), 1e-8f);
+      const float cm = __fdiv_rn(p.norm, scale);
+      int csum = 0;
+      if (live && token < p.rows_out) {
+        uint8_t* prow = p.packed + static_cast<int64_t>(token) * p.ld_packed + ip * 32;
+        int8_t* crow = p.codes ? p.codes + static_cast<int64_t>(token) * p.ld_codes + ip * 64 : nullptr;
+        csum = clamp ? quant_row64<true>(v, cm, lo, p.row_sums != nullptr, prow, crow)
+                     : quant_row64<false>(v, cm, lo, p.row_sums != nullptr, prow, crow);
+      }
+      if (p.row_sums) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, o);
+        if (lane == 0) rsum[par * 8 + idx] = csum;
+        named_bar_sync(bar_id, bar_cnt);
+      }
+      if (idx == first_w && lane == 0 && wtoken < p.rows_out) {
+        p.scales[wtoken] = scale;
+        if (p.row_sums) {
+          int tot = 0;
+          for (int w = 0; w < wpt; ++w) tot += rsum[par * 8 + first_w + w];
+          p.row_sums[wtoken] = tot;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == rp.mma_warp) {
+    if (lane == 0) mbar_wait(done, 0, nullptr);  // every issued MMA has retired
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kRqTmemCols);
+  }
+}
+
+}  // namespace dscq

@@ -147,9 +147,10 @@ class RowQuant:
 
 def rowquant(x: torch.Tensor, mode: str = "act_sym", clip: float = 1.0, rotate: bool = False,
              rows_out: int | None = None, KP: int | None = None, codes: bool = False,
-             row_sums: bool = False) -> RowQuant:
+             row_sums: bool = False, variant: str = "auto") -> RowQuant:
     """Per-row int4 quantisation of a 2-D CUDA tensor with an optional online Hadamard rotation
-    (y = x (H_a (x) H_b) / sqrt(K)), one fused kernel. See include/dscq_b200.h (dscq_rowquant)."""
+    (y = x (H_a (x) H_b) / sqrt(K)), one fused kernel. See include/dscq_b200.h (dscq_rowquant).
+    `variant`: "auto", "tc" (tcgen05 kernel) or "legacy" (CUDA-core kernels), for A/B timing."""
     if not x.is_cuda:
         raise RuntimeError("rowquant runs on CUDA tensors only")
     if x.dim() != 2 or x.stride(1) != 1:
@@ -169,9 +170,11 @@ def rowquant(x: torch.Tensor, mode: str = "act_sym", clip: float = 1.0, rotate: 
         sums = torch.empty((rows_out,), dtype=torch.int32, device=dev) if row_sums else None
         cds = torch.empty((rows_out, KP), dtype=torch.int8, device=dev) if codes else None
         a, h = rotation_factor(K, dev) if rotate else (1, None)
-        rc = _lib.load().dscq_rowquant(_ptr(x), _DT[x.dtype], M, K, x.stride(0), int(rotate), a, _ptr(h), m,
-                                       float(clip), rows_out, KP, _ptr(packed), KP // 2, _ptr(scales), _ptr(zeros),
-                                       _ptr(sums), _ptr(cds), KP if codes else 0, _stream(dev))
+        var = {"auto": _lib.QUANT_AUTO, "tc": _lib.QUANT_TC, "legacy": _lib.QUANT_LEGACY}[variant]
+        rc = _lib.load().dscq_rowquant_variant(_ptr(x), _DT[x.dtype], M, K, x.stride(0), int(rotate), a, _ptr(h), m,
+                                               float(clip), rows_out, KP, _ptr(packed), KP // 2, _ptr(scales),
+                                               _ptr(zeros), _ptr(sums), _ptr(cds), KP if codes else 0, var,
+                                               _stream(dev))
     _lib.check(rc, "rowquant")
     return RowQuant(packed, scales, zeros, sums, cds, KP)
 

@@ -46,6 +46,11 @@ extern "C" {
 #define DSCQ_GEMM_LARGE_M_PAIR 4   /* as LARGE_M, 256x256 tiles on CTA pairs (cta_group::2)  */
 #define DSCQ_GEMM_SMALL_M_TC 5     /* tcgen05 with weights on the 128-row MMA side (tokens as MMA N) */
 
+/* Rotate+quantize kernel choice (dscq_rowquant_variant `variant`) */
+#define DSCQ_QUANT_AUTO 0
+#define DSCQ_QUANT_TC 1         /* tcgen05: dense Hadamard factor on the tensor cores, WHT-64 in registers */
+#define DSCQ_QUANT_LEGACY 2     /* CUDA-core kernels (register WHT, mma.sync Kronecker, general)        */
+
 int dscq_version(void);
 const char* dscq_last_error(void);
 
@@ -89,6 +94,20 @@ int dscq_rowquant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x
                   const int8_t* h_a, int mode, float clip, int64_t rows_out, int64_t KP, uint8_t* packed,
                   int64_t ld_packed, float* scales, int32_t* zeros, int32_t* row_sums, int8_t* codes,
                   int64_t ld_codes, void* stream);
+
+/*
+ * dscq_rowquant with an explicit kernel choice (no counterpart in the reference):
+ *   DSCQ_QUANT_AUTO   as dscq_rowquant;
+ *   DSCQ_QUANT_TC     the tcgen05 rotate+quantize kernel (K = a' * 64 with a' <= 256,
+ *                     symmetric modes, bf16 input, KP == K, 16-byte aligned rows;
+ *                     DSCQ_ERR_UNSUPPORTED otherwise);
+ *   DSCQ_QUANT_LEGACY the CUDA-core kernels (register WHT / mma.sync Kronecker / general).
+ * All choices produce codes of the same rotation; the float summation order differs.
+ */
+int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x, int rotate, int rot_a,
+                          const int8_t* h_a, int mode, float clip, int64_t rows_out, int64_t KP, uint8_t* packed,
+                          int64_t ld_packed, float* scales, int32_t* zeros, int32_t* row_sums, int8_t* codes,
+                          int64_t ld_codes, int variant, void* stream);
 
 /*
  * Replaces matmul_cuda(a, b, sx, zx, sw, sums, bias, M, N, fused,

@@ -109,13 +109,16 @@ def _near_tie(q, tol=1e-3):
     return np.abs(np.abs(q - np.floor(q)) - 0.5) < tol
 
 
-@pytest.mark.parametrize("M,K", [(64, 4096), (32, 8192), (16, 11008), (16, 14336), (8, 28672), (3, 448)])
+@pytest.mark.parametrize("M,K", [(64, 4096), (33, 4096), (32, 8192), (16, 11008), (17, 11008), (16, 14336),
+                                 (5, 2048), (8, 28672), (3, 448), (6, 1024)])
 @pytest.mark.parametrize("mode", ["act_sym", "weight_sym"])
-def test_rowquant_rotated(oracle, cuda_device, M, K, mode):
+@pytest.mark.parametrize("variant", ["auto", "legacy"])
+def test_rowquant_rotated(oracle, cuda_device, M, K, mode, variant):
+    """auto routes K = a'*64 with 32 <= a' <= 256 to the tcgen05 kernel, the rest to the CUDA-core kernels."""
     from dscquant_b200 import ops
 
     x = synthetic.activations_bf16(M, K, seed=K) if mode == "act_sym" else synthetic.weights_bf16(M, K, seed=K)
-    r = ops.rowquant(_tbf(x, cuda_device), mode, rotate=True, KP=K, codes=True)
+    r = ops.rowquant(_tbf(x, cuda_device), mode, rotate=True, KP=K, codes=True, variant=variant)
     y = oracle.rotate(_f32(x))
     ref = oracle.quant_rows(y, MODES[mode], 1.0, KP=K)
     s_gpu = r.scales.cpu().numpy()
@@ -139,3 +142,34 @@ def test_rotation_preserves_norm_on_gpu_codes(oracle, cuda_device):
     deq = r.codes.cpu().numpy()[:, :4096].astype(np.float32) * r.scales.cpu().numpy()[:, None]
     rel = np.linalg.norm(deq - y) / np.linalg.norm(y)
     assert rel < 0.2
+
+
+@pytest.mark.parametrize("K", [1024, 2048, 4096, 8192, 11008, 14336])
+def test_rowquant_tc_against_legacy(cuda_device, K):
+    """tcgen05 kernel vs the CUDA-core kernels on the same rows, padding rows and code sums included:
+    codes equal except one-step differences at rounding boundaries, scales to 2e-6 relative,
+    packed bytes consistent with the codes, code sums exact, padding rows all zero."""
+    from dscquant_b200 import ops
+
+    M, rows_out = 301, 307
+    x = _tbf(synthetic.weights_bf16(M, K, seed=K + 1), cuda_device)
+    a = ops.rowquant(x, "weight_sym", rotate=True, KP=K, rows_out=rows_out, codes=True, row_sums=True, variant="tc")
+    b = ops.rowquant(x, "weight_sym", rotate=True, KP=K, rows_out=rows_out, codes=True, row_sums=True,
+                     variant="legacy")
+    torch.testing.assert_close(a.scales, b.scales, rtol=2e-6, atol=0)
+    ca, cb = a.codes.cpu().numpy().astype(np.int32), b.codes.cpu().numpy().astype(np.int32)
+    diff = ca != cb
+    assert np.all(np.abs(ca - cb)[diff] == 1) and diff.mean() < 1e-3
+    np.testing.assert_array_equal(a.row_sums.cpu().numpy(), ca.sum(1))
+    np.testing.assert_array_equal(ops.unpack_int4_cuda(a.packed, K).cpu().numpy().astype(np.int32), ca)
+    assert not ca[M:].any() and not a.packed[M:].any()
+
+
+def test_rowquant_tc_unsupported_shape_raises(cuda_device):
+    from dscquant_b200 import ops
+
+    x = torch.zeros((4, 448), dtype=torch.bfloat16, device=cuda_device)
+    with pytest.raises(RuntimeError):
+        ops.rowquant(x, "act_sym", rotate=True, KP=448, variant="tc")  # a' = 7 < 16
+    with pytest.raises(RuntimeError):
+        ops.rowquant(x.float(), "act_sym", rotate=True, KP=448, variant="tc")
