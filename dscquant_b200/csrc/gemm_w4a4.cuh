@@ -684,8 +684,10 @@ struct PairCfg {
   static constexpr int kRawStage = kRows * 64;      // 16 KB
   static constexpr int kExpHalf = 128 * 128;        // 16 KB
   static constexpr int kExpStage = kRows * 128;     // 32 KB
+  // A pair MMA (256 x 256 x 32) takes ~128 cycles; 4 expanded stages cover the leader -> peer ->
+  // leader signalling of a stage, the rest of the budget is raw (TMA) stages.
   static constexpr int ES = 4;
-  static constexpr int RS = 5;
+  static constexpr int RS = (212 * 1024 - ES * kExpStage - static_cast<int>(sizeof(EpiStage<256>))) / kRawStage;
   static constexpr int UPT = kRows * 4 / kExpandThreads;
   static constexpr int kTmemCols = 2 * BN;          // two accumulators x 256 columns
   static constexpr int kBarBytes = (2 * RS + 2 * ES + 5) * 8 + 16;
@@ -729,7 +731,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       mbar_init(&raw_empty[s], kExpandWarps);
     }
     for (int s = 0; s < ES; ++s) {
-      mbar_init(&exp_full[s], 2 * kExpandWarps);
+      // leader: its 8 expansion warps + one relayed arrival for the peer's 8; peer: its own 8
+      mbar_init(&exp_full[s], leader ? kExpandWarps + 1 : kExpandWarps);
       mbar_init(&exp_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -781,6 +784,21 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       }
     }
   } else if (warp == 8) {
+    // ------------------------------------------------ relay (peer): one cluster-scope arrival per
+    // stage on the leader once the peer's 8 expansion warps have arrived locally
+    if (!leader && lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < ntiles; tile += npairs)
+        for (int kb = 0; kb < kb_n; ++kb, ++g) {
+          const int s = g % ES;
+          if (!mbar_wait(&exp_full[s], (g / ES) & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_cluster(exp_full_ldr + static_cast<uint32_t>(s * 8));
+        }
+    }
     // ------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
       constexpr uint32_t idesc = umma_idesc_i8(256, BN);
@@ -848,7 +866,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&raw_empty[rs]);
-          mbar_arrive_cluster(exp_full_ldr + static_cast<uint32_t>(es * 8));
+          mbar_arrive(&exp_full[es]);  // local; the peer's relay forwards to the leader
         }
       }
     }
