@@ -17,6 +17,7 @@
 #include "wht_quant.cuh"
 #include "kron_quant.cuh"
 #include "gemv_w4a4.cuh"
+#include "gemm_a8.cuh"
 #include "rotq_tc.cuh"
 
 namespace {
@@ -111,6 +112,22 @@ int make_rows_map(CUtensorMap* map, const void* x, int64_t M, int ap, int64_t ld
   return DSCQ_OK;
 }
 
+// int8 activation codes [rows, cols] (row stride ld bytes) in 128 x 128-byte boxes landing with the
+// 128-byte swizzle: the K-major UMMA operand layout for the A8 GEMM.
+int make_i8_sw128_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {128u, 128u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled (int8 A) failed (" + std::to_string(r) + ")");
+  return DSCQ_OK;
+}
+
 int g_num_sms = 0;
 
 int num_sms() {
@@ -198,6 +215,20 @@ int launch_gemm_persistent(const CUtensorMap& tmP, const CUtensorMap& tmQ, const
   kern<<<grid, dscq::kPersistThreads, C::kSmemBytes, stream>>>(tmP, tmQ, gp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_persistent");
+  return DSCQ_OK;
+}
+
+template <int BN>
+int launch_gemm_a8(const CUtensorMap& tmA, const CUtensorMap& tmQ, const dscq::GemmParams& gp, cudaStream_t stream) {
+  using C = dscq::A8Cfg<BN>;
+  auto kern = dscq::w4a4_gemm_a8<BN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a4_gemm_a8)");
+  const int tiles = gp.tiles_i * gp.tiles_j;
+  const int grid = std::min(tiles, num_sms());
+  kern<<<grid, dscq::kPersistThreads, C::kSmemBytes, stream>>>(tmA, tmQ, gp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_a8");
   return DSCQ_OK;
 }
 
@@ -318,14 +349,14 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
                           int64_t ld_packed, float* scales, int32_t* zeros, int32_t* row_sums, int8_t* codes,
                           int64_t ld_codes, int variant, void* stream) {
   DSCQ_REQUIRE(variant >= DSCQ_QUANT_AUTO && variant <= DSCQ_QUANT_LEGACY, "unknown quantizer variant");
-  DSCQ_REQUIRE(x && packed && scales, "x, packed and scales must not be null");
+  DSCQ_REQUIRE(x && (packed || codes) && scales, "x, scales and packed or codes must not be null");
   DSCQ_REQUIRE(x_dtype == DSCQ_BF16 || x_dtype == DSCQ_F16 || x_dtype == DSCQ_F32, "x_dtype must be bf16/f16/f32");
   DSCQ_REQUIRE(M >= 1 && M <= (1 << 24), "require 1 <= M <= 2^24");
   DSCQ_REQUIRE(K >= 1 && K <= 32768, "require 1 <= K <= 32768");
   DSCQ_REQUIRE(ld_x >= K, "ld_x must be >= K");
   DSCQ_REQUIRE(rows_out >= M && rows_out <= (1 << 24), "rows_out must be >= M");
   DSCQ_REQUIRE(KP >= K && KP % 2 == 0 && KP <= 65536, "KP must be even and >= K");
-  DSCQ_REQUIRE(ld_packed >= KP / 2, "ld_packed must be >= KP/2");
+  DSCQ_REQUIRE(!packed || ld_packed >= KP / 2, "ld_packed must be >= KP/2");
   DSCQ_REQUIRE(mode >= DSCQ_ACT_SYM && mode <= DSCQ_ACT_ASYM_TORCH, "unknown quantizer mode");
   DSCQ_REQUIRE(std::isfinite(clip) && clip > 0.f, "clip must be a positive finite number");
   DSCQ_REQUIRE(!(mode == DSCQ_ACT_ASYM || mode == DSCQ_ACT_ASYM_TORCH) || zeros, "asymmetric modes need zeros");
@@ -369,7 +400,7 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   const bool sym = mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM;
   const int ap_tc = (rotate && log2b >= 6) ? static_cast<int>(K / 64) : 0;
   const bool tc_ok = rotate && log2b >= 6 && ap_tc >= 16 && ap_tc <= 256 && sym && x_dtype == DSCQ_BF16 &&
-                     KP == K && aligned(x, 16) && ld_x % 8 == 0 && aligned(packed, 16) && ld_packed % 16 == 0 &&
+                     KP == K && aligned(x, 16) && ld_x % 8 == 0 && (!packed || (aligned(packed, 16) && ld_packed % 16 == 0)) &&
                      (!codes || (aligned(codes, 16) && ld_codes % 16 == 0));
   if (variant == DSCQ_QUANT_TC && !tc_ok)
     return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize needs a rotation with K = a' * 64 (a' <= 256), a "
@@ -414,7 +445,7 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   }
   const bool fast = rotate && p.rot_a == 1 && log2b >= 10 && log2b <= 13 &&
                     (mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM) && x_dtype == DSCQ_BF16 && KP == K &&
-                    aligned(x, 16) && ld_x % 8 == 0 && aligned(packed, 2) && ld_packed % 2 == 0;
+                    aligned(x, 16) && ld_x % 8 == 0 && (!packed || (aligned(packed, 2) && ld_packed % 2 == 0));
   if (fast) {
     cudaError_t e = cudaSuccess;
     switch (log2b) {
@@ -588,6 +619,62 @@ int dscq_matmul_cols(const uint8_t* a, const uint8_t* b, const float* sx, const 
   DSCQ_REQUIRE(outs != nullptr && n_outs >= 1, "need at least one output buffer");
   return matmul_impl(a, b, sx, zx, sw, sums, bias, residual, M, N, KP, out_dtype, outs, n_outs, ld_out, col_off,
                      nullptr, variant, stream);
+}
+
+int dscq_matmul_a8(const int8_t* a, int64_t ld_a, const uint8_t* b, const float* sx, const float* sw, const void* bias,
+                   const void* residual, int64_t M, int64_t N, int64_t KP, int out_dtype, void* out, int32_t* raw,
+                   void* stream) {
+  DSCQ_REQUIRE(a && b && sx && sw, "a, b, sx and sw must not be null");
+  DSCQ_REQUIRE(out || raw, "at least one of out / raw must be given");
+  DSCQ_REQUIRE(M > 0 && M <= (1 << 24) && N > 0 && N <= (1 << 24) && KP > 0 && KP <= 1048576 && KP % 64 == 0,
+               "Invalid dimensions (need M, N > 0 and KP a positive multiple of 64)");
+  DSCQ_REQUIRE(ld_a >= KP && ld_a % 16 == 0, "ld_a must be >= KP and a multiple of 16");
+  DSCQ_REQUIRE(aligned(a, 16) && aligned(b, 16), "operands must be 16-byte aligned");
+  DSCQ_REQUIRE(out_dtype == DSCQ_BF16 || out_dtype == DSCQ_F16 || out_dtype == DSCQ_F32, "out_dtype must be bf16/f16/f32");
+  int st = check_device(nullptr);
+  if (st) return st;
+  const int64_t kbytes = KP / 2;
+  const int nsm = num_sms();
+  const int64_t ti = (M + 127) / 128;
+  const int64_t t256 = ti * ((N + 255) / 256), t128 = ti * ((N + 127) / 128);
+  auto eff = [&](int64_t t) { return static_cast<double>(t) / (((t + nsm - 1) / nsm) * nsm); };
+  const int BN = (t256 >= nsm / 2 && eff(t256) + 0.1 >= eff(t128)) ? 256 : 128;
+  const int64_t tj = (N + BN - 1) / BN;
+  DSCQ_REQUIRE(ti * tj * 8 < (int64_t(1) << 31), "problem too large");
+  CUtensorMap tmA, tmQ;
+  st = make_i8_sw128_map(&tmA, a, M, KP, ld_a);
+  if (st) return st;
+  st = make_u8_map(&tmQ, b, N, kbytes, kbytes, BN);
+  if (st) return st;
+  dscq::GemmParams gp;
+  gp.M = static_cast<int>(M);
+  gp.N = static_cast<int>(N);
+  gp.kblocks = static_cast<int>((KP + 127) / 128);
+  gp.tiles_i = static_cast<int>(ti);
+  gp.tiles_j = static_cast<int>(tj);
+  gp.splits = 1;
+  gp.sx = sx;
+  gp.zx = nullptr;
+  gp.sw = sw;
+  gp.wsum = nullptr;
+  gp.bias = bias;
+  gp.residual = residual;
+  gp.out = out;
+  gp.raw = raw;
+  gp.out_dtype = out_dtype;
+  gp.vec_out = (out != nullptr && N % 8 == 0 && aligned(out, 16)) ? 1 : 0;
+  gp.P = nullptr;
+  gp.Q = b;
+  gp.kbytes = static_cast<int>(kbytes);
+  gp.rowsP = static_cast<int>(M);
+  gp.rowsQ = static_cast<int>(N);
+  gp.ld_out = N;
+  gp.col_off = 0;
+  gp.n_outs = out ? 1 : 0;
+  for (int i = 0; i < 8; ++i) gp.outs[i] = nullptr;
+  gp.outs[0] = out;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return BN == 256 ? launch_gemm_a8<256>(tmA, tmQ, gp, s) : launch_gemm_a8<128>(tmA, tmQ, gp, s);
 }
 
 int dscq_pack_int4(const int8_t* codes, int64_t rows, int64_t K, int64_t ld_codes, uint8_t* packed,

@@ -209,7 +209,9 @@ __device__ __forceinline__ void epilogue_stage(const GemmParams& p, int tj, int 
   }
 }
 
-template <int BN>
+// SH: the accumulator holds 2^SH * sum(a * b) (8: both operands expanded as 16 * code; 4: int8
+// activation codes times expanded weights).
+template <int BN, int SH = 8>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int tj, uint32_t tmem_acc, int ew, int lane,
                                               const EpiStage<BN>* st, int par) {
   const int q = ew & 3, h = ew >> 2;
@@ -233,13 +235,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int t
       const int64_t r0 = static_cast<int64_t>(m) * p.N + n0;
 #pragma unroll
       for (int t = 0; t < 16; ++t)
-        if (n0 + t < p.N) p.raw[r0 + t] = static_cast<int32_t>(r[t]) >> 8;
+        if (n0 + t < p.N) p.raw[r0 + t] = static_cast<int32_t>(r[t]) >> SH;
     }
     if (!p.out) continue;
     float f[16];
 #pragma unroll
     for (int t = 0; t < 16; ++t) {
-      int32_t a = static_cast<int32_t>(r[t]) >> 8;
+      int32_t a = static_cast<int32_t>(r[t]) >> SH;
       if (asym) a += zc * st->wsum[par][c0 + t];
       f[t] = epi_scale(a, sxm, st->sw[par][c0 + t]);
       if (has_bias) f[t] = __fadd_rn(f[t], st->bias[par][c0 + t]);

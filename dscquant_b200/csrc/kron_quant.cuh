@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(AP * 2) kron_quant(const RowQuantParams p, int
     const float cm = __fdiv_rn(p.norm, scale);
 
     // ---- codes, packed bytes (k = i*64 + 8n + 2q + e -> byte i*32 + 4n + q)
-    uint8_t* prow = p.packed + static_cast<int64_t>(row) * p.ld_packed;
+    uint8_t* prow = p.packed ? p.packed + static_cast<int64_t>(row) * p.ld_packed : nullptr;
     int8_t* crow = p.codes ? p.codes + static_cast<int64_t>(row) * p.ld_codes : nullptr;
     int csum = 0;
 #pragma unroll
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(AP * 2) kron_quant(const RowQuantParams p, int
           }
           const uint32_t c0 = __float_as_uint(q0 + 12582912.f) & 15u;
           const uint32_t c1 = __float_as_uint(q1 + 12582912.f) & 15u;
-          prow[i * 32 + 4 * n + q] = static_cast<uint8_t>(c0 | (c1 << 4));
+          if (prow) prow[i * 32 + 4 * n + q] = static_cast<uint8_t>(c0 | (c1 << 4));
           if (crow || p.row_sums) {
             const int s0 = static_cast<int>(c0 << 28) >> 28, s1 = static_cast<int>(c1 << 28) >> 28;
             csum += s0 + s1;

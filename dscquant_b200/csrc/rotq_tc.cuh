@@ -105,8 +105,8 @@ __device__ __forceinline__ uint32_t bfi4(uint32_t src, uint32_t base, uint32_t p
   return d;
 }
 
-// Codes of 64 values -> 32 packed bytes (even k in the low nibble) at prow;
-// optional int8 codes at crow; returns the code sum when SUMS.
+// Codes of 64 values -> 32 packed bytes (even k in the low nibble) at prow (if
+// not null); optional int8 codes at crow; returns the code sum when SUMS.
 template <bool SUMS, bool CLAMP>
 __device__ __forceinline__ int quant_store64(const float2 (&u)[32], float cm, float lo, uint8_t* prow, int8_t* crow) {
   uint32_t w[8];
@@ -130,9 +130,11 @@ __device__ __forceinline__ int quant_store64(const float2 (&u)[32], float cm, fl
     }
     w[j] = word;
   }
-  uint4* dst = reinterpret_cast<uint4*>(prow);
-  dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-  dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  if (prow) {
+    uint4* dst = reinterpret_cast<uint4*>(prow);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
   if (crow) {
     uint32_t cw[16];
 #pragma unroll
@@ -381,7 +383,7 @@ __global__ void __launch_bounds__(kRqMaxThreads, 1)
       const float cm = __fdiv_rn(p.norm, scale);
       int csum = 0;
       if (live && token < p.rows_out) {
-        uint8_t* prow = p.packed + static_cast<int64_t>(token) * p.ld_packed + ip * 32;
+        uint8_t* prow = p.packed ? p.packed + static_cast<int64_t>(token) * p.ld_packed + ip * 32 : nullptr;
         int8_t* crow = p.codes ? p.codes + static_cast<int64_t>(token) * p.ld_codes + ip * 64 : nullptr;
         csum = clamp ? quant_row64<true>(v, cm, lo, p.row_sums != nullptr, prow, crow)
                      : quant_row64<false>(v, cm, lo, p.row_sums != nullptr, prow, crow);

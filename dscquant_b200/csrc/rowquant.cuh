@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(T) rowquant_smem(const RowQuantParams p) {
 
   int csum = 0;
   const int pad_code = asym ? zero : 0;
-  uint8_t* prow = p.packed + static_cast<int64_t>(row) * p.ld_packed;
+  uint8_t* prow = p.packed ? p.packed + static_cast<int64_t>(row) * p.ld_packed : nullptr;
   int8_t* crow = p.codes ? p.codes + static_cast<int64_t>(row) * p.ld_codes : nullptr;
   for (int pr = threadIdx.x; pr < p.KP / 2; pr += T) {
     const int k = 2 * pr;
@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(T) rowquant_smem(const RowQuantParams p) {
     const int c1 = k + 1 < K ? quant_code(src[k + 1], scale, zero, p.mode) : pad_code;
     if (k < K) csum += c0;
     if (k + 1 < K) csum += c1;
-    prow[pr] = static_cast<uint8_t>(nibble_of(c0, p.mode) | (nibble_of(c1, p.mode) << 4));
+    if (prow) prow[pr] = static_cast<uint8_t>(nibble_of(c0, p.mode) | (nibble_of(c1, p.mode) << 4));
     if (crow) {
       crow[k] = static_cast<int8_t>(c0);
       crow[k + 1] = static_cast<int8_t>(c1);

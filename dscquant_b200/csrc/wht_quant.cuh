@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(128) wht_quant_pow2(const RowQuantParams p) {
 
   int csum = 0;
   if (active) {
-    uint8_t* prow = p.packed + static_cast<int64_t>(row) * p.ld_packed;
+    uint8_t* prow = p.packed ? p.packed + static_cast<int64_t>(row) * p.ld_packed : nullptr;
     int8_t* crow = p.codes ? p.codes + static_cast<int64_t>(row) * p.ld_codes : nullptr;
 #pragma unroll
     for (int j = 0; j < G; ++j) {
@@ -175,11 +175,13 @@ __global__ void __launch_bounds__(128) wht_quant_pow2(const RowQuantParams p) {
           }
         }
       }
-      uint8_t* dst = prow + (E / 2) * j + (g0 >> 1);
-      if constexpr (GPT == 4)
-        *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(bytes);
-      else
-        *dst = static_cast<uint8_t>(bytes);
+      if (prow) {
+        uint8_t* dst = prow + (E / 2) * j + (g0 >> 1);
+        if constexpr (GPT == 4)
+          *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(bytes);
+        else
+          *dst = static_cast<uint8_t>(bytes);
+      }
     }
     if (t == 0) p.scales[row] = scale;
   }

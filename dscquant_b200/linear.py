@@ -109,6 +109,12 @@ class QuantLinear(nn.Module):
         self._prep = dict(packed=q.packed, sw=q.scales, wsum=q.row_sums, bias=bias, K=K, N=N, KP=KP,
                           aclip=float(self.activation_clip), bias_cache={})
 
+    # int8_activations = True: above A8_MIN_TOKENS tokens the symmetric scheme hands the GEMM int8
+    # activation codes (w4a4_gemm_a8) instead of packed nibbles. Same output bits; measured on par with
+    # the packed kernel on B200, so it is off by default.
+    int8_activations = False
+    A8_MIN_TOKENS = 64
+
     # ------------------------------------------------------------------ packed-weight format
     PREPARED_FORMAT = "dscq-w4a4-v1"
 
@@ -160,17 +166,24 @@ class QuantLinear(nn.Module):
         x2 = x.reshape(-1, K)
         if x2.stride(-1) != 1:
             x2 = x2.contiguous()
-        mode = "act_sym" if self.symmetric else "act_asym_torch"
-        q = ops.rowquant(x2, mode, clip=p["aclip"], rotate=self.rotate, KP=p["KP"])
         bias = None
         if p["bias"] is not None:
             bias = p["bias_cache"].get(x.dtype)
             if bias is None:
                 bias = p["bias"].to(x.dtype).contiguous()
                 p["bias_cache"][x.dtype] = bias
-        y = ops.w4a4_gemm(q.packed, p["packed"], q.scales, p["sw"], M=x2.shape[0], N=N,
-                          zx=None if self.symmetric else q.zeros, sums=None if self.symmetric else p["wsum"],
-                          bias=bias, out_dtype=x.dtype)
+        M = x2.shape[0]
+        if self.symmetric and self.int8_activations and M > self.A8_MIN_TOKENS:
+            # int8 activation codes straight into the GEMM's TMA (no activation expansion); same bits
+            q = ops.rowquant(x2, "act_sym", clip=p["aclip"], rotate=self.rotate, KP=p["KP"], codes=True,
+                             packed_out=False)
+            y = ops.w4a4_gemm_a8(q.codes, p["packed"], q.scales, p["sw"], M=M, N=N, bias=bias, out_dtype=x.dtype)
+        else:
+            mode = "act_sym" if self.symmetric else "act_asym_torch"
+            q = ops.rowquant(x2, mode, clip=p["aclip"], rotate=self.rotate, KP=p["KP"])
+            y = ops.w4a4_gemm(q.packed, p["packed"], q.scales, p["sw"], M=M, N=N,
+                              zx=None if self.symmetric else q.zeros, sums=None if self.symmetric else p["wsum"],
+                              bias=bias, out_dtype=x.dtype)
         return y.reshape(*x.shape[:-1], N)
 
     def extra_repr(self) -> str:

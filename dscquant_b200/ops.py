@@ -147,10 +147,11 @@ class RowQuant:
 
 def rowquant(x: torch.Tensor, mode: str = "act_sym", clip: float = 1.0, rotate: bool = False,
              rows_out: int | None = None, KP: int | None = None, codes: bool = False,
-             row_sums: bool = False, variant: str = "auto") -> RowQuant:
+             row_sums: bool = False, variant: str = "auto", packed_out: bool = True) -> RowQuant:
     """Per-row int4 quantisation of a 2-D CUDA tensor with an optional online Hadamard rotation
     (y = x (H_a (x) H_b) / sqrt(K)), one fused kernel. See include/dscq_b200.h (dscq_rowquant).
-    `variant`: "auto", "tc" (tcgen05 kernel) or "legacy" (CUDA-core kernels), for A/B timing."""
+    `variant`: "auto", "tc" (tcgen05 kernel) or "legacy" (CUDA-core kernels), for A/B timing.
+    `packed_out=False` (with codes=True) writes only the int8 codes, the A operand of w4a4_gemm_a8."""
     if not x.is_cuda:
         raise RuntimeError("rowquant runs on CUDA tensors only")
     if x.dim() != 2 or x.stride(1) != 1:
@@ -164,7 +165,9 @@ def rowquant(x: torch.Tensor, mode: str = "act_sym", clip: float = 1.0, rotate: 
     asym = m in (_lib.ACT_ASYM, _lib.ACT_ASYM_TORCH)
     dev = x.device
     with torch.cuda.device(dev):
-        packed = torch.empty((rows_out, KP // 2), dtype=torch.uint8, device=dev)
+        if not packed_out and not codes:
+            raise ValueError("rowquant needs packed_out or codes")
+        packed = torch.empty((rows_out, KP // 2), dtype=torch.uint8, device=dev) if packed_out else None
         scales = torch.empty((rows_out,), dtype=torch.float32, device=dev)
         zeros = torch.empty((rows_out,), dtype=torch.int32, device=dev) if asym else None
         sums = torch.empty((rows_out,), dtype=torch.int32, device=dev) if row_sums else None
@@ -172,7 +175,8 @@ def rowquant(x: torch.Tensor, mode: str = "act_sym", clip: float = 1.0, rotate: 
         a, h = rotation_factor(K, dev) if rotate else (1, None)
         var = {"auto": _lib.QUANT_AUTO, "tc": _lib.QUANT_TC, "legacy": _lib.QUANT_LEGACY}[variant]
         rc = _lib.load().dscq_rowquant_variant(_ptr(x), _DT[x.dtype], M, K, x.stride(0), int(rotate), a, _ptr(h), m,
-                                               float(clip), rows_out, KP, _ptr(packed), KP // 2, _ptr(scales),
+                                               float(clip), rows_out, KP, _ptr(packed), KP // 2 if packed_out else 0,
+                                               _ptr(scales),
                                                _ptr(zeros), _ptr(sums), _ptr(cds), KP if codes else 0, var,
                                                _stream(dev))
     _lib.check(rc, "rowquant")
@@ -203,6 +207,29 @@ def w4a4_gemm(a: torch.Tensor, b: torch.Tensor, sx: torch.Tensor, sw: torch.Tens
         rc = _lib.load().dscq_matmul(_ptr(a), _ptr(b), _ptr(sx), _ptr(zx), _ptr(sw), _ptr(sums), _ptr(bias),
                                      _ptr(residual), M, N, KP, _DT[out_dtype], _ptr(out), _ptr(raw), v, _stream(dev))
     _lib.check(rc, "w4a4_gemm")
+    return (out, raw) if return_raw else out
+
+
+def w4a4_gemm_a8(a: torch.Tensor, b: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor, *, M: int | None = None,
+                 N: int | None = None, bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+                 out_dtype: torch.dtype = torch.bfloat16, return_raw: bool = False):
+    """w4a4_gemm with int8 activation codes a [M, KP] (values in [-8, 7], e.g. rowquant(..., codes=True,
+    packed_out=False)) and packed int4 weights b [N, KP/2]; symmetric activations only. Same bits as
+    w4a4_gemm on the packed form of a."""
+    M = a.size(0) if M is None else M
+    N = b.size(0) if N is None else N
+    KP = b.size(1) * 2
+    for name, t in (("b", b), ("sx", sx), ("sw", sw)):
+        _check_cuda(t, name)
+    if not a.is_cuda or a.dtype != torch.int8 or a.dim() != 2 or a.stride(1) != 1 or a.size(1) < KP:
+        raise RuntimeError("a must be CUDA int8 codes [M, >= KP] with unit column stride")
+    dev = a.device
+    with torch.cuda.device(dev):
+        out = torch.empty((M, N), dtype=out_dtype, device=dev)
+        raw = torch.empty((M, N), dtype=torch.int32, device=dev) if return_raw else None
+        rc = _lib.load().dscq_matmul_a8(_ptr(a), a.stride(0), _ptr(b), _ptr(sx), _ptr(sw), _ptr(bias), _ptr(residual),
+                                        M, N, KP, _DT[out_dtype], _ptr(out), _ptr(raw), _stream(dev))
+    _lib.check(rc, "matmul_a8")
     return (out, raw) if return_raw else out
 
 

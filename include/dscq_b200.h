@@ -85,7 +85,7 @@ int dscq_quantize(const void* x, int x_dtype, int64_t M, int64_t K, float clip, 
  *   (NULL when a == 1).
  * mode: DSCQ_ACT_SYM / DSCQ_WEIGHT_SYM / DSCQ_ACT_ASYM / DSCQ_ACT_ASYM_TORCH.
  * Writes rows_out (>= M) rows; KP (even, >= K) packed columns:
- *   packed [rows_out, ld_packed >= KP/2], scales [rows_out],
+ *   packed [rows_out, ld_packed >= KP/2] (may be NULL when codes is given), scales [rows_out],
  *   zeros [rows_out] (asym modes, may be NULL otherwise),
  *   row_sums [rows_out] (sum of codes over k < K, may be NULL),
  *   codes [rows_out, ld_codes >= KP] int8 (may be NULL).
@@ -125,6 +125,19 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
 int dscq_matmul(const uint8_t* a, const uint8_t* b, const float* sx, const int32_t* zx, const float* sw,
                 const int32_t* sums, const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP,
                 int out_dtype, void* out, int32_t* raw, int variant, void* stream);
+
+/*
+ * dscq_matmul with int8 activation codes (no counterpart in the reference, whose
+ * activations are packed nibbles): a [M, ld_a >= KP] int8 codes in [-8, 7] (the
+ * codes output of dscq_rowquant in a symmetric mode, ld_a a multiple of 16),
+ * b [N, KP/2] packed int4 weights. Symmetric activations only (no zero points):
+ *   out[m, n] = (sum_k a[m,k] b[n,k]) * sx[m] * sw[n] + bias[n] + residual[m, n]
+ * Same result bits as dscq_matmul on the packed form of a; one byte per
+ * activation element instead of half, one third less expansion work per K block.
+ */
+int dscq_matmul_a8(const int8_t* a, int64_t ld_a, const uint8_t* b, const float* sx, const float* sw, const void* bias,
+                   const void* residual, int64_t M, int64_t N, int64_t KP, int out_dtype, void* out, int32_t* raw,
+                   void* stream);
 
 /*
  * Column-block form of dscq_matmul (no counterpart in the reference, which has

@@ -167,3 +167,47 @@ def test_no_device_errors_raised(cuda_device):
     from dscquant_b200 import ops
 
     assert ops.device_status(cuda_device) == 0
+
+
+@pytest.mark.parametrize("M,N,KP", [(1, 128, 128), (130, 260, 192), (1024, 2304, 1024), (1000, 2200, 448),
+                                    (2048, 4096, 256), (300, 1000, 2048), (64, 384, 1024), (384, 5120, 4096),
+                                    (700, 300, 64)])
+def test_gemm_a8_exact(oracle, cuda_device, M, N, KP):
+    """int8-activation GEMM: accumulators bit-exact vs the oracle on the packed form of the same codes,
+    outputs bit-exact vs the oracle epilogue and vs the packed-activation kernel."""
+    from dscquant_b200 import ops
+
+    rng = np.random.default_rng(M * 3 + N + KP)
+    codes = rng.integers(-8, 8, (M, KP)).astype(np.int8)
+    a_packed = oracle.pack_int4(codes)
+    b = _packed(rng, N, KP)
+    sx = (rng.random(M, dtype=np.float32) * 0.1 + 1e-3).astype(np.float32)
+    sw = (rng.random(N, dtype=np.float32) * 0.01 + 1e-4).astype(np.float32)
+    tb = oracle.f32_to_bf16_bits(rng.standard_normal(N).astype(np.float32))
+    T = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(cuda_device)  # noqa: E731
+    bias = torch.from_numpy(tb.view(np.int16)).view(torch.bfloat16).to(cuda_device)
+    out, raw = ops.w4a4_gemm_a8(T(codes), T(b), T(sx), T(sw), bias=bias, return_raw=True)
+    ref_raw = oracle.gemm_s4(a_packed, b, M, N, KP)
+    np.testing.assert_array_equal(raw.cpu().numpy(), ref_raw)
+    ref = oracle.epilogue(ref_raw, sx, sw, bias=bias.float().cpu().numpy())
+    np.testing.assert_array_equal(_bf16_bits(out), oracle.f32_to_bf16_bits(ref))
+    out_p = ops.w4a4_gemm(T(a_packed), T(b), T(sx), T(sw), bias=bias)
+    assert torch.equal(out, out_p)
+
+
+def test_gemm_a8_strided_codes_and_errors(oracle, cuda_device):
+    """Codes with a padded row stride (a view into a wider buffer) and the argument checks."""
+    from dscquant_b200 import ops
+
+    rng = np.random.default_rng(3)
+    M, N, KP = 200, 256, 512
+    wide = torch.from_numpy(rng.integers(-8, 8, (M, KP + 64)).astype(np.int8)).to(cuda_device)
+    codes = wide[:, :KP]
+    b = torch.from_numpy(_packed(rng, N, KP)).to(cuda_device)
+    sx = torch.rand(M, device=cuda_device)
+    sw = torch.rand(N, device=cuda_device)
+    out, raw = ops.w4a4_gemm_a8(codes, b, sx, sw, return_raw=True)
+    ref_raw = oracle.gemm_s4(oracle.pack_int4(codes.cpu().numpy()), b.cpu().numpy(), M, N, KP)
+    np.testing.assert_array_equal(raw.cpu().numpy(), ref_raw)
+    with pytest.raises(RuntimeError):
+        ops.w4a4_gemm_a8(codes.to(torch.int32), b, sx, sw)

@@ -180,3 +180,18 @@ def test_host_pipeline_matches_forward(cuda_device):
             assert torch.equal(h, r)
     with pytest.raises(ValueError):
         pipe.run(mods, [t.clone() for t in h_in], h_out)  # not pinned
+
+
+def test_int8_activation_path_same_bits(cuda_device):
+    """QuantLinear with int8_activations (A8 GEMM above 64 tokens) returns the packed path's bits."""
+    from dscquant_b200 import QuantConfig, QuantLinear
+
+    K, N = 4096, 512
+    w = synthetic.weights_bf16(N, K, seed=12)
+    ql = QuantLinear(_linear(w, None, cuda_device), QuantConfig())
+    ql.enabled = True
+    x = torch.randn(300, K, device=cuda_device, dtype=torch.bfloat16)
+    y_packed = ql(x)
+    ql.int8_activations = True
+    y_a8 = ql(x)
+    assert torch.equal(y_packed, y_a8)

@@ -173,3 +173,17 @@ def test_rowquant_tc_unsupported_shape_raises(cuda_device):
         ops.rowquant(x, "act_sym", rotate=True, KP=448, variant="tc")  # a' = 7 < 16
     with pytest.raises(RuntimeError):
         ops.rowquant(x.float(), "act_sym", rotate=True, KP=448, variant="tc")
+
+
+@pytest.mark.parametrize("K", [4096, 11008, 448])
+def test_rowquant_codes_only(cuda_device, K):
+    """packed_out=False writes the same int8 codes (and scales) without the packed bytes."""
+    from dscquant_b200 import ops
+
+    x = _tbf(synthetic.activations_bf16(77, K, seed=K + 3), cuda_device)
+    a = ops.rowquant(x, "act_sym", rotate=True, KP=K, codes=True)
+    b = ops.rowquant(x, "act_sym", rotate=True, KP=K, codes=True, packed_out=False)
+    assert b.packed is None
+    assert torch.equal(a.codes, b.codes) and torch.equal(a.scales, b.scales)
+    with pytest.raises(ValueError):
+        ops.rowquant(x, "act_sym", rotate=True, KP=K, packed_out=False)
