@@ -187,19 +187,19 @@ cudaError_t launch_kron(const dscq::RowQuantParams& p, int a, int s, cudaStream_
   return cudaGetLastError();
 }
 
-template <int MT>
+template <int MT, int G>
 cudaError_t launch_rotq(const CUtensorMap& tm, const dscq::RotqParams& rp, cudaStream_t st) {
   // at least 120 KB so that one CTA (which allocates all 512 TMEM columns) occupies an SM
   const size_t smem = std::max<size_t>(1024 + rp.a_bytes + static_cast<size_t>(rp.ns) * rp.stage_bytes + 1024,
                                        120 * 1024);
-  cudaError_t e = cudaFuncSetAttribute(dscq::rotq_tc<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(dscq::rotq_tc<MT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const int grid = std::min(rp.groups, num_sms());
   const int nwarps = std::max(rp.tma_warp, rp.mma_warp) + 1;
   const int threads = std::max(nwarps, (rp.nteam - 1) * rp.team_stride + rp.tw) * 32;
-  if (threads > dscq::kRqMaxThreads) return cudaErrorInvalidConfiguration;
-  dscq::rotq_tc<MT><<<grid, threads, smem, st>>>(tm, rp);
+  if (threads > dscq::RqThreads<MT>::value) return cudaErrorInvalidConfiguration;
+  dscq::rotq_tc<MT, G><<<grid, threads, smem, st>>>(tm, rp);
   return cudaGetLastError();
 }
 
@@ -399,13 +399,16 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   // tcgen05 path: K = a' * 64, a' <= 256, symmetric modes, bf16 rows, 16-byte aligned outputs
   const bool sym = mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM;
   const int ap_tc = (rotate && log2b >= 6) ? static_cast<int>(K / 64) : 0;
-  const bool tc_ok = rotate && log2b >= 6 && ap_tc >= 16 && ap_tc <= 256 && sym && x_dtype == DSCQ_BF16 &&
+  const bool tc_ok = rotate && log2b >= 6 && ap_tc >= 16 && ap_tc <= 224 && sym && x_dtype == DSCQ_BF16 &&
                      KP == K && aligned(x, 16) && ld_x % 8 == 0 && (!packed || (aligned(packed, 16) && ld_packed % 16 == 0)) &&
                      (!codes || (aligned(codes, 16) && ld_codes % 16 == 0));
   if (variant == DSCQ_QUANT_TC && !tc_ok)
-    return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize needs a rotation with K = a' * 64 (a' <= 256), a "
+    return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize needs a rotation with K = a' * 64 (a' <= 224), a "
                                       "symmetric mode, bf16 input, KP == K and 16-byte aligned rows");
-  if (tc_ok && (variant == DSCQ_QUANT_TC || (variant == DSCQ_QUANT_AUTO && ap_tc >= 32))) {
+  // AUTO: the tcgen05 kernel has a longer fixed prologue (TMEM, Hadamard operand) and wins once
+  // there is enough work: from 4096 rows, or from 1024 rows when the dense factor is larger than 64
+  const bool tc_auto = ap_tc >= 32 && (rows_out >= 4096 || (ap_tc > 64 && rows_out >= 1024));
+  if (tc_ok && (variant == DSCQ_QUANT_TC || (variant == DSCQ_QUANT_AUTO && tc_auto))) {
     dscq::RotqParams rp;
     rp.p = p;
     rp.a_base = p.rot_a;
@@ -421,12 +424,16 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
     rp.a_bytes = static_cast<uint32_t>(rp.mt * rp.nkb * 16384);
     rp.stage_bytes = static_cast<uint32_t>(rp.P * rp.ap16 * 128);
     rp.ns = std::min<int>(dscq::kRqMaxStages, (210 * 1024 - static_cast<int>(rp.a_bytes)) / static_cast<int>(rp.stage_bytes));
-    if (rp.mt == 1) {  // three teams of four warps (lane quadrants 0-3), then the TMA and MMA warps
+    // one MMA spans G token blocks: G = 4 (N = 256) with one M tile, 2 (N = 128) with two; the
+    // stage ring holds whole groups
+    const int G = rp.mt == 1 ? 4 : 2;
+    rp.ns = rp.ns / G * G;
+    if (rp.mt == 1) {  // two teams of four warps (lane quadrants 0-3), then the TMA and MMA warps
       rp.tw = 4;
       rp.team_stride = 4;
-      rp.nteam = 3;
-      rp.tma_warp = 12;
-      rp.mma_warp = 13;
+      rp.nteam = 2;
+      rp.tma_warp = 8;
+      rp.mma_warp = 9;
     } else {  // two teams of 4 + ceil((a' - 128) / 32) warps at warps 0.. and 8..
       rp.tw = 4 + (rp.ap - 128 + 31) / 32;
       rp.team_stride = 8;
@@ -439,7 +446,7 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
     CUtensorMap tm;
     st = make_rows_map(&tm, x, M, rp.ap, ld_x, rp.ap16, rp.P);
     if (st) return st;
-    cudaError_t e = rp.mt == 1 ? launch_rotq<1>(tm, rp, cst) : launch_rotq<2>(tm, rp, cst);
+    cudaError_t e = rp.mt == 1 ? launch_rotq<1, 4>(tm, rp, cst) : launch_rotq<2, 2>(tm, rp, cst);
     if (e != cudaSuccess) return cuda_fail(e, "launch rotq_tc");
     return DSCQ_OK;
   }

@@ -235,6 +235,18 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr) {
   return d;
 }
 
+// MN-major 128-byte-swizzled operand spanning several 64-element MN atoms:
+// LBO = byte stride between MN atoms, SBO = 1024 (8-row k groups).
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn_atoms(uint32_t smem_addr, uint32_t atom_stride) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((atom_stride >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16 with bf16 A and B, f32 D; A K-major,
 // B MN-major (bit 16), N>>3 at [17,23), M>>4 at [24,29).
 __host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int m, int n) {

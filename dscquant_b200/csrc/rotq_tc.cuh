@@ -35,7 +35,6 @@
 
 namespace dscq {
 
-constexpr int kRqMaxThreads = 576;
 constexpr int kRqTmemCols = 512;
 constexpr int kRqMaxStages = 12;
 constexpr int kRqMaxTeams = 4;
@@ -161,15 +160,25 @@ __device__ __forceinline__ int quant_row64(const float2 (&u)[32], float cm, floa
   return sums ? quant_store64<true, CLAMP>(u, cm, lo, prow, crow) : quant_store64<false, CLAMP>(u, cm, lo, prow, crow);
 }
 
+// Threads per CTA: 10 warps for one M tile (two teams of 4 + TMA + MMA), up to 16 for two
+// (two teams of up to 7 for a' <= 224, TMA, MMA).
 template <int MT>
-__global__ void __launch_bounds__(kRqMaxThreads, 1)
+struct RqThreads {
+  static constexpr int value = MT == 1 ? 320 : 512;
+};
+
+template <int MT, int G>
+__global__ void __launch_bounds__(RqThreads<MT>::value, 1)
     rotq_tc(const __grid_constant__ CUtensorMap tmX, const RotqParams rp) {
   const RowQuantParams& p = rp.p;
   extern __shared__ uint8_t rq_smem_dyn[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rq_smem_dyn) + 1023) & ~uintptr_t(1023));
   uint8_t* a_base = smem;
   uint8_t* b_base = smem + rp.a_bytes;
-  constexpr int S = kRqTmemCols / (MT * 64);  // TMEM slots (token groups in flight)
+  // One MMA covers G consecutive B stages (token blocks) as its N = 64 G columns (MN atoms at the
+  // stage stride): an M = 128 tcgen05.mma costs about the same for N = 64 and N = 256.
+  constexpr int SLOT = MT * 64 * G;              // TMEM columns per MMA group
+  constexpr int S = kRqTmemCols / SLOT;          // TMEM slots (MMA groups in flight)
   uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + rp.ns * rp.stage_bytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + kRqMaxStages;
@@ -303,28 +312,33 @@ __global__ void __launch_bounds__(kRqMaxThreads, 1)
       }
     }
   } else if (warp == rp.mma_warp) {
-    // ------------------------------------------------ MMA issuer
+    // ------------------------------------------------ MMA issuer: groups of G token blocks
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16_bmn(128, 64);
+      constexpr uint32_t idesc = umma_idesc_bf16_bmn(128, 64 * G);
       const uint32_t a0 = smem_u32(a_base);
-      int n = 0;
-      const bool a_ok = mbar_wait(aready, 0, abort_flag);
-      for (int g = blockIdx.x; a_ok && g < groups; g += gridDim.x, ++n) {
-        const int s = n % ns, slot = n % S, use = n / S;
+      const int my_blocks = groups > static_cast<int>(blockIdx.x)
+                                ? (groups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                                      static_cast<int>(gridDim.x)
+                                : 0;
+      bool ok = mbar_wait(aready, 0, abort_flag);
+      for (int q = 0; ok && q * G < my_blocks; ++q) {
+        const int slot = q % S, use = q / S, n0 = q * G;
+        const int nb = min(G, my_blocks - n0);  // blocks of this group that were loaded
         if (use > 0 && !mbar_wait(&tempty[slot], (use - 1) & 1u, abort_flag)) break;
-        if (!mbar_wait(&full[s], (n / ns) & 1u, abort_flag)) break;
+        for (int b = 0; ok && b < nb; ++b) ok = mbar_wait(&full[(n0 + b) % ns], ((n0 + b) / ns) & 1u, abort_flag);
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t b0 = smem_u32(b_base + s * rp.stage_bytes);
+        const uint32_t b0 = smem_u32(b_base + (n0 % ns) * rp.stage_bytes);  // ns % G == 0: contiguous stages
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          const uint32_t d = tmem_base + static_cast<uint32_t>(slot * MT * 64 + m * 64);
+          const uint32_t d = tmem_base + static_cast<uint32_t>(slot * SLOT + m * 64 * G);
           for (int ks = 0; ks < rp.ksteps; ++ks) {
             const uint64_t ad = umma_desc_sw128(a0 + (m * rp.nkb + (ks >> 2)) * 16384 + (ks & 3) * 32);
-            const uint64_t bd = umma_desc_sw128_mn(b0 + ks * 2048);
+            const uint64_t bd = umma_desc_sw128_mn_atoms(b0 + ks * 2048, rp.stage_bytes);
             umma_f16_ss(d, ad, bd, idesc, ks > 0 ? 1u : 0u);
           }
         }
-        umma_commit(&empty[s]);
+        for (int b = 0; b < nb; ++b) umma_commit(&empty[(n0 + b) % ns]);
         umma_commit(&tfull[slot]);
       }
       umma_commit(done);
@@ -353,55 +367,66 @@ __global__ void __launch_bounds__(kRqMaxThreads, 1)
     const int bar_cnt = tw * 32;
     float* rmax = red_max + team * 16;
     int* rsum = red_sum + team * 16;
-    int n = team, it = 0;
-    for (int g = blockIdx.x + team * gridDim.x; g < groups; g += rp.nteam * gridDim.x, n += rp.nteam, ++it) {
-      const int slot = n % S, use = n / S, par = it & 1;
+    const int my_blocks = groups > static_cast<int>(blockIdx.x)
+                              ? (groups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                                    static_cast<int>(gridDim.x)
+                              : 0;
+    int it = 0;
+    for (int q = team; q * G < my_blocks; q += rp.nteam) {
+      const int slot = q % S, use = q / S, n0 = q * G;
+      const int nblk = min(G, my_blocks - n0);
       bool ok = mbar_wait(&tfull[slot], use & 1u, abort_flag);
       ok = named_bar_and(bar_id, bar_cnt, ok && !*abort_flag);
       if (!ok) break;
       tc_fence_after();
-      float2 v[32];
-      tmem_ld64(tmem_base + (static_cast<uint32_t>(qd * 32) << 16) + static_cast<uint32_t>(slot * MT * 64 + mtile * 64),
-                v);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[slot]);  // this slot's columns may be overwritten
-
-      wht64_regs(v);
-      float amax = live ? absmax64(v) : 0.f;
-#pragma unroll
-      for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      if (lane == 0) rmax[par * 8 + idx] = amax;
-      named_bar_sync(bar_id, bar_cnt);
-      amax = 0.f;
-      for (int w = 0; w < wpt; ++w) amax = fmaxf(amax, rmax[par * 8 + first_w + w]);
-
-      const int token = g * P + (MT == 1 ? pr : 0);
-      const int wtoken = g * P + wtok;
-      const float amax_y = __fmul_rn(amax, p.norm);
-      const float scale = fmaxf(__fdiv_rn(__fmul_rn(amax_y, p.clip), 7.f), 1e-8f);
-      const float cm = __fdiv_rn(p.norm, scale);
-      int csum = 0;
-      if (live && token < p.rows_out) {
-        uint8_t* prow = p.packed ? p.packed + static_cast<int64_t>(token) * p.ld_packed + ip * 32 : nullptr;
-        int8_t* crow = p.codes ? p.codes + static_cast<int64_t>(token) * p.ld_codes + ip * 64 : nullptr;
-        csum = clamp ? quant_row64<true>(v, cm, lo, p.row_sums != nullptr, prow, crow)
-                     : quant_row64<false>(v, cm, lo, p.row_sums != nullptr, prow, crow);
-      }
-      if (p.row_sums) {
-#pragma unroll
-        for (int o = 16; o; o >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, o);
-        if (lane == 0) rsum[par * 8 + idx] = csum;
-        named_bar_sync(bar_id, bar_cnt);
-      }
-      if (idx == first_w && lane == 0 && wtoken < p.rows_out) {
-        p.scales[wtoken] = scale;
-        if (p.row_sums) {
-          int tot = 0;
-          for (int w = 0; w < wpt; ++w) tot += rsum[par * 8 + first_w + w];
-          p.row_sums[wtoken] = tot;
+      for (int b = 0; b < nblk; ++b, ++it) {
+        const int g = blockIdx.x + (n0 + b) * gridDim.x;  // token block
+        const int par = it & 1;
+        float2 v[32];
+        tmem_ld64(tmem_base + (static_cast<uint32_t>(qd * 32) << 16) +
+                      static_cast<uint32_t>(slot * SLOT + mtile * 64 * G + b * 64),
+                  v);
+        if (b == nblk - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[slot]);  // the group's columns may be overwritten
         }
-      }
+        wht64_regs(v);
+        float amax = live ? absmax64(v) : 0.f;
+  #pragma unroll
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (lane == 0) rmax[par * 8 + idx] = amax;
+        named_bar_sync(bar_id, bar_cnt);
+        amax = 0.f;
+        for (int w = 0; w < wpt; ++w) amax = fmaxf(amax, rmax[par * 8 + first_w + w]);
+
+        const int token = g * P + (MT == 1 ? pr : 0);
+        const int wtoken = g * P + wtok;
+        const float amax_y = __fmul_rn(amax, p.norm);
+        const float scale = fmaxf(__fdiv_rn(__fmul_rn(amax_y, p.clip), 7.f), 1e-8f);
+        const float cm = __fdiv_rn(p.norm, scale);
+        int csum = 0;
+        if (live && token < p.rows_out) {
+          uint8_t* prow = p.packed ? p.packed + static_cast<int64_t>(token) * p.ld_packed + ip * 32 : nullptr;
+          int8_t* crow = p.codes ? p.codes + static_cast<int64_t>(token) * p.ld_codes + ip * 64 : nullptr;
+          csum = clamp ? quant_row64<true>(v, cm, lo, p.row_sums != nullptr, prow, crow)
+                       : quant_row64<false>(v, cm, lo, p.row_sums != nullptr, prow, crow);
+        }
+        if (p.row_sums) {
+  #pragma unroll
+          for (int o = 16; o; o >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, o);
+          if (lane == 0) rsum[par * 8 + idx] = csum;
+          named_bar_sync(bar_id, bar_cnt);
+        }
+        if (idx == first_w && lane == 0 && wtoken < p.rows_out) {
+          p.scales[wtoken] = scale;
+          if (p.row_sums) {
+            int tot = 0;
+            for (int w = 0; w < wpt; ++w) tot += rsum[par * 8 + first_w + w];
+            p.row_sums[wtoken] = tot;
+          }
+        }
+      }  // blocks of the group
     }
   }
 

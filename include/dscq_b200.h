@@ -98,7 +98,7 @@ int dscq_rowquant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x
 /*
  * dscq_rowquant with an explicit kernel choice (no counterpart in the reference):
  *   DSCQ_QUANT_AUTO   as dscq_rowquant;
- *   DSCQ_QUANT_TC     the tcgen05 rotate+quantize kernel (K = a' * 64 with a' <= 256,
+ *   DSCQ_QUANT_TC     the tcgen05 rotate+quantize kernel (K = a' * 64 with 16 <= a' <= 224,
  *                     symmetric modes, bf16 input, KP == K, 16-byte aligned rows;
  *                     DSCQ_ERR_UNSUPPORTED otherwise);
  *   DSCQ_QUANT_LEGACY the CUDA-core kernels (register WHT / mma.sync Kronecker / general).

@@ -112,9 +112,11 @@ def _near_tie(q, tol=1e-3):
 @pytest.mark.parametrize("M,K", [(64, 4096), (33, 4096), (32, 8192), (16, 11008), (17, 11008), (16, 14336),
                                  (5, 2048), (8, 28672), (3, 448), (6, 1024)])
 @pytest.mark.parametrize("mode", ["act_sym", "weight_sym"])
-@pytest.mark.parametrize("variant", ["auto", "legacy"])
+@pytest.mark.parametrize("variant", ["auto", "tc", "legacy"])
 def test_rowquant_rotated(oracle, cuda_device, M, K, mode, variant):
-    """auto routes K = a'*64 with 32 <= a' <= 256 to the tcgen05 kernel, the rest to the CUDA-core kernels."""
+    """tc: the tcgen05 kernel (K = a'*64, 16 <= a' <= 224); legacy: the CUDA-core kernels; auto picks by size."""
+    if variant == "tc" and not (K % 64 == 0 and 16 <= K // 64 <= 224):
+        pytest.skip("outside the tcgen05 kernel's range")
     from dscquant_b200 import ops
 
     x = synthetic.activations_bf16(M, K, seed=K) if mode == "act_sym" else synthetic.weights_bf16(M, K, seed=K)
