@@ -128,13 +128,25 @@ __global__ void __launch_bounds__(T) rowquant_smem(const RowQuantParams p) {
     }
     if (p.rot_a > 1 && p.rot_a <= 32) {
       // Dense factor, in place, one column c per thread: Y[i2, c] = sum_i H_a[i, i2] * Z[i, c].
+      // The signs of column i2 of H_a sit in shared memory as one 32-bit mask per i2 (bit i set
+      // where H_a[i, i2] < 0); every thread reads the same word (broadcast).
+      __shared__ uint32_t hneg[32];
       const int a = p.rot_a;
+      if (threadIdx.x < a) {
+        uint32_t m = 0;
+        for (int i = 0; i < a; ++i) m |= static_cast<uint32_t>(p.h_a[i * a + threadIdx.x] < 0) << i;
+        hneg[threadIdx.x] = m;
+      }
+      __syncthreads();
       for (int c = threadIdx.x; c < b; c += T) {
         float v[32];
-        for (int i = 0; i < a; ++i) v[i] = buf[(i << p.log2b) + c];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = i < a ? buf[(i << p.log2b) + c] : 0.f;
         for (int i2 = 0; i2 < a; ++i2) {
+          const uint32_t m = hneg[i2];
           float acc = 0.f;
-          for (int i = 0; i < a; ++i) acc = p.h_a[i * a + i2] > 0 ? acc + v[i] : acc - v[i];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc += ((m >> i) & 1u) ? -v[i] : v[i];
           buf[(i2 << p.log2b) + c] = acc;
         }
       }

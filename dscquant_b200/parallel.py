@@ -9,13 +9,17 @@ bit-identical to the same columns of a single-GPU QuantLinear.
 
 Exchange of the blocks (the only cross-device step):
 
-* ``fused`` (default): the [M, N] output lives in symmetric memory
-  (torch.distributed._symmetric_memory); the GEMM epilogue of every rank stores
-  each output tile into the output buffer of *every* rank at its column offset
-  (dscq_matmul_cols with the peers' pointers: plain stores over NVLink), so the
-  all-gather happens tile by tile inside the GEMM and no transpose pass is
-  needed. Two symmetric-memory barriers per call: before the GEMM (no rank
-  overwrites a buffer a peer is still reading) and after it (all blocks landed).
+* ``fused`` (default): the input rows are split across the ranks for the
+  rotate+quantize (each rank quantises M/p token rows into a symmetric buffer
+  and then copies the other ranks' packed rows and scales over NVLink), and the
+  [M, N] output lives in symmetric memory (torch.distributed._symmetric_memory):
+  the GEMM epilogue of every rank stores each output tile into the output
+  buffer of *every* rank at its column offset (dscq_matmul_cols with the peers'
+  pointers: plain stores over NVLink), so the all-gather happens tile by tile
+  inside the GEMM and no transpose pass is needed. Three symmetric-memory
+  barriers per call: before the quantisation (no rank overwrites a buffer a
+  peer is still reading), after it (all row blocks written) and after the GEMM
+  (all output blocks landed).
 * ``nccl``: local [M, N/p] block, ``all_gather_into_tensor`` into [p, M, N/p],
   then one copy into the [M, N] layout.
 """
@@ -35,6 +39,14 @@ def shard_bounds(N: int, world: int, rank: int) -> tuple[int, int]:
         raise ValueError(f"N={N} is not divisible by the group size {world}")
     step = N // world
     return rank * step, (rank + 1) * step
+
+
+def row_bounds(M: int, world: int, rank: int) -> tuple[int, int]:
+    """Token rows [lo, hi) this rank quantises in the fused mode (ceil(M/p) per rank, the last ranks
+    may get fewer or none)."""
+    step = (M + world - 1) // world
+    lo = min(M, rank * step)
+    return lo, min(M, lo + step)
 
 
 def assemble(blocks: torch.Tensor) -> torch.Tensor:
@@ -69,10 +81,19 @@ class ColumnParallelQuantLinear:
         if mode == "fused":
             import torch.distributed._symmetric_memory as symm_mem
 
+            g = group if group is not None else dist.group.WORLD
             self.out = symm_mem.empty((max_tokens, N), dtype=torch.bfloat16, device=self.device)
-            self.hdl = symm_mem.rendezvous(self.out, group if group is not None else dist.group.WORLD)
+            self.hdl = symm_mem.rendezvous(self.out, g)
             ptrs = list(self.hdl.buffer_ptrs)
             self.peer_ptrs = (ctypes.c_void_p * len(ptrs))(*ptrs)
+            # quantised activations: each rank writes its own token rows, then reads the others'
+            self.a_sym = symm_mem.empty((max_tokens, self.KP // 2), dtype=torch.uint8, device=self.device)
+            self.a_hdl = symm_mem.rendezvous(self.a_sym, g)
+            self.s_sym = symm_mem.empty((max_tokens,), dtype=torch.float32, device=self.device)
+            self.s_hdl = symm_mem.rendezvous(self.s_sym, g)
+            self.a_peer = [self.a_hdl.get_buffer(r, (max_tokens, self.KP // 2), torch.uint8) for r in range(self.world)]
+            self.s_peer = [self.s_hdl.get_buffer(r, (max_tokens,), torch.float32) for r in range(self.world)]
+            self.h_rot = ops.rotation_factor(self.K, self.device) if rotate else (1, None)
 
     def _local_block(self, q, M: int) -> torch.Tensor:
         return ops.w4a4_gemm(q.packed, self.w_packed, q.scales, self.sw, M=M, N=self.hi - self.lo, bias=self.bias)
@@ -81,19 +102,43 @@ class ColumnParallelQuantLinear:
         if not x.is_cuda or x.dtype != torch.bfloat16:
             raise RuntimeError("ColumnParallelQuantLinear expects a bf16 CUDA input")
         M = x.shape[0]
-        q = ops.rowquant(x.contiguous(), "act_sym", rotate=self.rotate, KP=self.KP)
         if self.mode == "nccl":
+            q = ops.rowquant(x.contiguous(), "act_sym", rotate=self.rotate, KP=self.KP)
             block = self._local_block(q, M)
             gathered = torch.empty((self.world, M, self.hi - self.lo), dtype=block.dtype, device=block.device)
             dist.all_gather_into_tensor(gathered, block, group=self.group)
             return assemble(gathered)
         if M > self.max_tokens:
             raise RuntimeError(f"M={M} exceeds max_tokens={self.max_tokens} of the symmetric output buffer")
-        self.hdl.barrier(channel=0)
-        rc = _lib.load().dscq_matmul_cols(ops._ptr(q.packed), ops._ptr(self.w_packed), ops._ptr(q.scales), None,
+        q = self._quantize_rows_sharded(x.contiguous(), M)
+        rc = _lib.load().dscq_matmul_cols(ops._ptr(q[0]), ops._ptr(self.w_packed), ops._ptr(q[1]), None,
                                          ops._ptr(self.sw), None, ops._ptr(self.bias), None, M, self.hi - self.lo,
                                          self.KP, _lib.BF16, self.peer_ptrs, self.world, self.N, self.lo, 0,
                                          ops._stream(self.device))
         _lib.check(rc, "dscq_matmul_cols")
-        self.hdl.barrier(channel=1)
+        self.hdl.barrier(channel=2)
         return self.out[:M]
+
+    def _quantize_rows_sharded(self, x: torch.Tensor, M: int):
+        """Fused mode: rank r rotates and quantises token rows row_bounds(M, p, r) into its symmetric
+        buffers, then copies the other ranks' packed rows and scales over NVLink (peer reads), so every
+        rank holds the full packed activations after 1/p of the quantisation work."""
+        self.hdl.barrier(channel=0)  # every rank is done reading last call's buffers
+        lo, hi = row_bounds(M, self.world, self.rank)
+        if hi > lo:
+            a, h = self.h_rot
+            rows = x[lo:hi]
+            rc = _lib.load().dscq_rowquant(ops._ptr(rows), _lib.BF16, hi - lo, self.K, x.stride(0), int(self.rotate), a,
+                                          ops._ptr(h), _lib.ACT_SYM, 1.0, hi - lo, self.KP,
+                                          ops._ptr(self.a_sym[lo:hi]), self.KP // 2, ops._ptr(self.s_sym[lo:hi]),
+                                          None, None, None, 0, ops._stream(self.device))
+            _lib.check(rc, "rowquant")
+        self.hdl.barrier(channel=1)  # all row blocks written
+        for r in range(self.world):
+            if r == self.rank:
+                continue
+            rlo, rhi = row_bounds(M, self.world, r)
+            if rhi > rlo:
+                self.a_sym[rlo:rhi].copy_(self.a_peer[r][rlo:rhi], non_blocking=True)
+                self.s_sym[rlo:rhi].copy_(self.s_peer[r][rlo:rhi], non_blocking=True)
+        return self.a_sym, self.s_sym

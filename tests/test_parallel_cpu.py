@@ -76,3 +76,14 @@ def test_shard_bounds():
     full = parallel.assemble(blocks)
     assert full.shape == (3, 8)
     assert torch.equal(full[:, 4:], blocks[1]) and torch.equal(full[:, :4], blocks[0])
+
+
+def test_row_bounds_cover_all_rows():
+    from dscquant_b200 import parallel
+
+    for M in (1, 2, 5, 300, 4096, 4097):
+        for world in (1, 2, 3, 4, 8):
+            spans = [parallel.row_bounds(M, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == M
+            assert all(lo <= hi for lo, hi in spans)
+            assert all(spans[r][1] == spans[r + 1][0] for r in range(world - 1))
