@@ -256,7 +256,7 @@ int launch_gemm_pair(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq:
   const int pairs = std::min(tiles, num_sms() / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
-  cfg.blockDim = dim3(dscq::kPersistThreads);
+  cfg.blockDim = dim3(dscq::kPairThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

@@ -190,6 +190,8 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int ti, int tj, 
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kPersistThreads = 576;  // 8 epilogue + 2 control + 8 expansion warps
+constexpr int kPairThreads = 608;     // + one more relay warp (pair kernel)
+constexpr int kPairRelays = 2;        // peer warps forwarding stage arrivals to the leader
 
 template <int BN>
 struct EpiStage {
@@ -698,7 +700,7 @@ struct PairCfg {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-__global__ void __launch_bounds__(kPersistThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     w4a4_gemm_pair(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                    const GemmParams p) {
   using C = PairCfg;
@@ -785,24 +787,22 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         for (int j = g > RS ? g - RS : 0; j < g; ++j) mbar_wait(&raw_full[j % RS], (j / RS) & 1u, nullptr);
       }
     }
-  } else if (warp == 8) {
-    // ------------------------------------------------ relay (peer): one cluster-scope arrival per
-    // stage on the leader once the peer's 8 expansion warps have arrived locally
+  } else if (warp == 8 || warp == 18) {
+    // ------------------------------------------------ relays (peer): one cluster-scope arrival per
+    // stage on the leader once the peer's 8 expansion warps have arrived locally. A release
+    // arrival at cluster scope holds its thread for a while, so kPairRelays warps (8 and 18) take
+    // alternate K blocks and their latencies overlap.
     if (!leader && lane == 0) {
-      int g = 0;
-      bool ok = true;
-      for (int tile = pair; ok && tile < ntiles; tile += npairs)
-        for (int kb = 0; kb < kb_n; ++kb, ++g) {
-          const int s = g % ES;
-          if (!mbar_wait(&exp_full[s], (g / ES) & 1u, abort_flag)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_cluster(exp_full_ldr + static_cast<uint32_t>(s * 8));
-        }
+      const int r = warp == 8 ? 0 : 1;
+      const int total = (ntiles > pair ? (ntiles - pair + npairs - 1) / npairs : 0) * kb_n;
+      for (int g = r; g < total; g += kPairRelays) {
+        const int s = g % ES;
+        if (!mbar_wait(&exp_full[s], (g / ES) & 1u, abort_flag)) break;
+        mbar_arrive_cluster(exp_full_ldr + static_cast<uint32_t>(s * 8));
+      }
     }
     // ------------------------------------------------ MMA issuer (leader only)
-    if (leader && lane == 0) {
+    if (warp == 8 && leader && lane == 0) {
       constexpr uint32_t idesc = umma_idesc_i8(256, BN);
       const uint32_t exp_empty_peer = dsmem_map(smem_u32(exp_empty), 1);
       const uint32_t tmem_full_peer = dsmem_map(smem_u32(tmem_full), 1);
