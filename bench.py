@@ -602,7 +602,7 @@ def main():
                        "parallelism": f"dp{world} over tokens" if world > 1 else "single GPU",
                        "l2": f"{R} layer replicas cycled (working set > 126 MB L2)"},
             "gpu_launches": 11 * args.steps,
-            "roofline": {"kernel": "w4a4_gemm_persistent", "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
+            "roofline": {"kernel": "w4a4_gemm_pair", "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
                          "unit": "TFLOP/s", "frac": gemm_tops / int8_peak, "traffic": traffic,
                          "traffic_note": "bytes per launch, ncu capture at M=2048 (profiles/)",
                          "peak_note": f"int8 dense = 2 x {peaks['source']} bf16 cuBLAS {peaks['bf16_tflops']} TFLOP/s; "

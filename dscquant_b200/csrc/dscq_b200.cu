@@ -558,7 +558,9 @@ static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, cons
   const int64_t rowsP = swap ? N : M, rowsQ = swap ? M : N;
   st = make_u8_map(&tmP, P, rowsP, kbytes, kbytes, 128);
   if (st) return st;
-  const bool pair = persistent && BN == 256 && variant == DSCQ_GEMM_LARGE_M_PAIR;
+  // AUTO takes the CTA-pair kernel whenever the 256-wide tile is chosen (2-SM MMAs); LARGE_M keeps
+  // the 1-CTA persistent kernel for A/B timing
+  const bool pair = persistent && BN == 256 && (variant == DSCQ_GEMM_LARGE_M_PAIR || variant == DSCQ_GEMM_AUTO);
   st = make_u8_map(&tmQ, Q, rowsQ, kbytes, kbytes, pair ? 128 : BN);
   if (st) return st;
 

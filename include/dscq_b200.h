@@ -41,9 +41,9 @@ extern "C" {
 /* GEMM variants (dscq_matmul `variant`) */
 #define DSCQ_GEMM_AUTO 0
 #define DSCQ_GEMM_SMALL_M 1     /* decode kernel for M <= 32, else the SMALL_M_TC path */
-#define DSCQ_GEMM_LARGE_M 2     /* activations on the 128-row MMA side              */
+#define DSCQ_GEMM_LARGE_M 2     /* 1-CTA persistent kernel, activations on the 128-row MMA side */
 #define DSCQ_GEMM_LARGE_M_DIRECT 3 /* as LARGE_M, operands loaded to registers (A/B timing) */
-#define DSCQ_GEMM_LARGE_M_PAIR 4   /* as LARGE_M, 256x256 tiles on CTA pairs (cta_group::2)  */
+#define DSCQ_GEMM_LARGE_M_PAIR 4   /* 256x256 tiles on CTA pairs (cta_group::2); AUTO's choice for large M */
 #define DSCQ_GEMM_SMALL_M_TC 5     /* tcgen05 with weights on the 128-row MMA side (tokens as MMA N) */
 
 /* Rotate+quantize kernel choice (dscq_rowquant_variant `variant`) */
