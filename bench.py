@@ -583,7 +583,7 @@ def main():
                "sample": f"{rows} tokens x 7 layer linears per step, {n} steps, oracle C W4A4 linear "
                          "(rotation, symmetric int4 codes, int32 GEMM, epilogue) with pthreads"}
 
-    # DRAM bytes per GEMM launch from one ncu capture of each benchmark shape at M = 2048
+    # DRAM bytes per w4a4_gemm_pair launch from one ncu capture of each benchmark shape at M = 2048
     # (dram__bytes_read.sum + dram__bytes_write.sum), launch-weighted over the step's 7 GEMMs
     traffic = None
     if M == 2048:
@@ -604,7 +604,7 @@ def main():
             "gpu_launches": 11 * args.steps,
             "roofline": {"kernel": "w4a4_gemm_pair", "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
                          "unit": "TFLOP/s", "frac": gemm_tops / int8_peak, "traffic": traffic,
-                         "traffic_note": "bytes per launch, ncu capture at M=2048 (profiles/)",
+                         "traffic_note": "w4a4_gemm_pair bytes per launch, ncu capture of each shape at M=2048 (profiles/)",
                          "peak_note": f"int8 dense = 2 x {peaks['source']} bf16 cuBLAS {peaks['bf16_tflops']} TFLOP/s; "
                                       "ops are integer ops (2 per MAC)",
                          "share_of_step": gemm_ms / elapsed_ms},
