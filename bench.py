@@ -59,7 +59,8 @@ def parse():
     p.add_argument("--N", type=int, default=11008)
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--variant", type=int, default=0,
-                   help="--kernel-case gemm: dscq_matmul variant 0-5, or 6 = dscq_matmul_a8 (int8 activation codes)")
+                   help="--kernel-case gemm: dscq_matmul variant 0-5, or dscq_matmul_a8 (int8 activation codes): "
+                        "6 = AUTO (CTA pairs), 7 = the 1-CTA kernel")
     p.add_argument("--qvariant", default="auto", choices=["auto", "tc", "legacy"],
                    help="rotate+quantize kernel for --kernel-case quant")
     p.add_argument("--graph", action="store_true",
@@ -124,7 +125,7 @@ def kernel_case(args) -> None:
     else:
         w = bf(synthetic.weights_bf16(args.N, args.K, seed=2))
         qw = ops.rowquant(w, "weight_sym", rotate=True, KP=args.K)
-        qx = ops.rowquant(x, "act_sym", rotate=True, KP=args.K, codes=args.variant == 6)
+        qx = ops.rowquant(x, "act_sym", rotate=True, KP=args.K, codes=args.variant in (6, 7))
         out = torch.empty((args.M, args.N), dtype=torch.bfloat16, device=dev)
         from dscquant_b200 import _lib
 
@@ -135,10 +136,12 @@ def kernel_case(args) -> None:
         lib = _lib.load()
 
         def fn(i=0):
-            if args.variant == 6:  # int8 activation codes (dscq_matmul_a8)
-                _lib.check(lib.dscq_matmul_a8(ops._ptr(qx.codes), args.K, ops._ptr(wcopies[i % copies]),
-                                              ops._ptr(qx.scales), ops._ptr(qw.scales), None, None, args.M, args.N,
-                                              args.K, _lib.BF16, ops._ptr(out), None, ops._stream(dev)), "matmul_a8")
+            if args.variant in (6, 7):  # int8 activation codes: AUTO (CTA pairs) / the 1-CTA kernel
+                v = _lib.GEMM_AUTO if args.variant == 6 else _lib.GEMM_LARGE_M
+                _lib.check(lib.dscq_matmul_a8_variant(ops._ptr(qx.codes), args.K, ops._ptr(wcopies[i % copies]),
+                                                      ops._ptr(qx.scales), ops._ptr(qw.scales), None, None, args.M,
+                                                      args.N, args.K, _lib.BF16, ops._ptr(out), None, v,
+                                                      ops._stream(dev)), "matmul_a8")
                 return
             _lib.check(lib.dscq_matmul(ops._ptr(qx.packed), ops._ptr(wcopies[i % copies]), ops._ptr(qx.scales), None,
                                        ops._ptr(qw.scales), None, None, None, args.M, args.N, args.K,

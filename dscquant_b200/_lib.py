@@ -36,6 +36,8 @@ SIGNATURES = {
                                      _i64, _vp, _vp, _vp, _vp, _i64, _i32, _vp]),
     "dscq_matmul": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i32, _vp]),
     "dscq_matmul_a8": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp]),
+    "dscq_matmul_a8_variant": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i32,
+                                      _vp]),
     "dscq_matmul_cols": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32,
                                 ctypes.POINTER(ctypes.c_void_p), _i32, _i64, _i64, _i32, _vp]),
     "dscq_pack_int4": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),

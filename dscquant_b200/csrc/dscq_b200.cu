@@ -271,6 +271,31 @@ int launch_gemm_pair(const CUtensorMap& tmP, const CUtensorMap& tmQ, const dscq:
   return DSCQ_OK;
 }
 
+int launch_gemm_pair_a8(const CUtensorMap& tmA, const CUtensorMap& tmQ, const dscq::GemmParams& gp,
+                        cudaStream_t stream) {
+  using C = dscq::PairA8Cfg<DSCQ_PAIR_A8_ES, DSCQ_PAIR_A8_RS>;
+  auto kern = dscq::w4a4_gemm_pair_a8<DSCQ_PAIR_A8_ES, DSCQ_PAIR_A8_RS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a4_gemm_pair_a8)");
+  const int tiles = ((gp.M + 255) / 256) * gp.tiles_j;
+  const int pairs = std::min(tiles, num_sms() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(dscq::kPairA8Threads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, tmA, tmQ, gp);
+  if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_pair_a8");
+  return DSCQ_OK;
+}
+
 int launch_gemv(const dscq::GemmParams& gp, cudaStream_t stream) {
   const unsigned grid = static_cast<unsigned>((gp.N + 15) / 16);
   const int nt = (gp.M + 7) / 8;
@@ -633,6 +658,15 @@ int dscq_matmul_cols(const uint8_t* a, const uint8_t* b, const float* sx, const 
 int dscq_matmul_a8(const int8_t* a, int64_t ld_a, const uint8_t* b, const float* sx, const float* sw, const void* bias,
                    const void* residual, int64_t M, int64_t N, int64_t KP, int out_dtype, void* out, int32_t* raw,
                    void* stream) {
+  return dscq_matmul_a8_variant(a, ld_a, b, sx, sw, bias, residual, M, N, KP, out_dtype, out, raw, DSCQ_GEMM_AUTO,
+                                stream);
+}
+
+int dscq_matmul_a8_variant(const int8_t* a, int64_t ld_a, const uint8_t* b, const float* sx, const float* sw,
+                           const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP, int out_dtype,
+                           void* out, int32_t* raw, int variant, void* stream) {
+  DSCQ_REQUIRE(variant == DSCQ_GEMM_AUTO || variant == DSCQ_GEMM_LARGE_M || variant == DSCQ_GEMM_LARGE_M_PAIR,
+               "dscq_matmul_a8 variant must be AUTO, LARGE_M or LARGE_M_PAIR");
   DSCQ_REQUIRE(a && b && sx && sw, "a, b, sx and sw must not be null");
   DSCQ_REQUIRE(out || raw, "at least one of out / raw must be given");
   DSCQ_REQUIRE(M > 0 && M <= (1 << 24) && N > 0 && N <= (1 << 24) && KP > 0 && KP <= 1048576 && KP % 64 == 0,
@@ -647,13 +681,15 @@ int dscq_matmul_a8(const int8_t* a, int64_t ld_a, const uint8_t* b, const float*
   const int64_t ti = (M + 127) / 128;
   const int64_t t256 = ti * ((N + 255) / 256), t128 = ti * ((N + 127) / 128);
   auto eff = [&](int64_t t) { return static_cast<double>(t) / (((t + nsm - 1) / nsm) * nsm); };
-  const int BN = (t256 >= nsm / 2 && eff(t256) + 0.1 >= eff(t128)) ? 256 : 128;
+  const int BN = variant == DSCQ_GEMM_LARGE_M_PAIR || (t256 >= nsm / 2 && eff(t256) + 0.1 >= eff(t128)) ? 256 : 128;
+  // LARGE_M keeps the 1-CTA kernel; AUTO and LARGE_M_PAIR take the CTA-pair kernel for 256-wide tiles
+  const bool pair = BN == 256 && variant != DSCQ_GEMM_LARGE_M;
   const int64_t tj = (N + BN - 1) / BN;
   DSCQ_REQUIRE(ti * tj * 8 < (int64_t(1) << 31), "problem too large");
   CUtensorMap tmA, tmQ;
   st = make_i8_sw128_map(&tmA, a, M, KP, ld_a);
   if (st) return st;
-  st = make_u8_map(&tmQ, b, N, kbytes, kbytes, BN);
+  st = make_u8_map(&tmQ, b, N, kbytes, kbytes, pair ? 128 : BN);
   if (st) return st;
   dscq::GemmParams gp;
   gp.M = static_cast<int>(M);
@@ -683,6 +719,7 @@ int dscq_matmul_a8(const int8_t* a, int64_t ld_a, const uint8_t* b, const float*
   for (int i = 0; i < 8; ++i) gp.outs[i] = nullptr;
   gp.outs[0] = out;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (pair) return launch_gemm_pair_a8(tmA, tmQ, gp, s);
   return BN == 256 ? launch_gemm_a8<256>(tmA, tmQ, gp, s) : launch_gemm_a8<128>(tmA, tmQ, gp, s);
 }
 

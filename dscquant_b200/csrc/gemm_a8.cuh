@@ -236,4 +236,264 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
   }
 }
 
+// ============================================================ CTA pairs with int8 activation codes
+// 256 x 256 output tiles on a cluster of two CTAs issuing tcgen05.mma.cta_group::2 (M = 256), as in
+// w4a4_gemm_pair, but with int8 activation codes: each CTA's 128 activation rows of a K block
+// arrive by a cta_group::2 TMA load whose bytes complete on the LEADER's a_full barrier, so the
+// activation half needs neither expansion nor a relayed arrival. Only the 128 weight rows of
+// each CTA are expanded (natural k order, 16 * code); the peer's expansion is forwarded to the
+// leader by two relay warps. Per K block and CTA the shared memory moves 16 KB (activation TMA)
+// + 8 KB (weight TMA) + 8 KB read / 16 KB written by the expansion + 32 KB of MMA operand reads,
+// against 96 KB in the packed-activation pair kernel.
+//
+// Roles (640 threads): warps 0-7 epilogue; warp 8 MMA issuer (leader) or relay 0 (peer);
+// warp 9 activation TMA; warps 10-17 weight expansion; warp 18 relay 1 (peer); warp 19 weight TMA.
+constexpr int kPairA8Threads = 640;
+
+#ifndef DSCQ_PAIR_A8_ES
+#define DSCQ_PAIR_A8_ES 5
+#endif
+#ifndef DSCQ_PAIR_A8_RS
+#define DSCQ_PAIR_A8_RS 7
+#endif
+
+template <int ES_, int RS_>
+struct PairA8Cfg {
+  static constexpr int BN = 256;
+  static constexpr int ES = ES_;                       // operand stages (activations + expanded weights)
+  static constexpr int RS = RS_;                       // packed weight stages
+  static constexpr int kAStage = 128 * 128;            // this CTA's 128 activation rows x 128 K (int8)
+  static constexpr int kBStage = 128 * 128;            // this CTA's 128 weight rows x 128 K (expanded)
+  static constexpr int kStage = kAStage + kBStage;
+  static constexpr int kRawStage = 128 * 64;           // this CTA's 128 weight rows x 128 K (packed)
+  static constexpr int UPT = 128 * 4 / kExpandThreads;  // 16-byte raw chunks per expansion thread
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kBarBytes = (2 * RS + 3 * ES + 5) * 8 + 16;
+  static constexpr int kEpiBytes = static_cast<int>(sizeof(EpiStage<BN>));
+  static constexpr int kSmemBytes = 1024 + ES * kStage + RS * kRawStage + kBarBytes + kEpiBytes;
+  static_assert(ES >= 2 && RS >= 2, "need two stages of each ring");
+  static_assert(128 * 4 % kExpandThreads == 0, "expansion chunks must divide evenly");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+template <int ES, int RS>
+__global__ void __launch_bounds__(kPairA8Threads, 1)
+    w4a4_gemm_pair_a8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ,
+                      const GemmParams p) {
+  using C = PairA8Cfg<ES, RS>;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_base = smem;  // stage s: activations at +0, expanded weights at +kAStage
+  uint8_t* raw_base = smem + ES * C::kStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw_base + RS * C::kRawStage);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = bars + RS;
+  uint64_t* a_full = bars + 2 * RS;      // leader: one armed arrival + both CTAs' activation bytes
+  uint64_t* exp_full = a_full + ES;      // leader: 8 expansion warps + the relayed peer arrival; peer: 8
+  uint64_t* st_empty = exp_full + ES;    // both: the leader's MMA commit
+  uint64_t* tmem_full = st_empty + ES;   // [2] both: the leader's MMA commit
+  uint64_t* tmem_empty = tmem_full + 2;  // [2] leader: 2 x 8 epilogue warps
+  uint64_t* mma_done = tmem_full + 4;    // [1] both
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  EpiStage<BN>* est = reinterpret_cast<EpiStage<BN>*>(reinterpret_cast<uint8_t*>(bars) + C::kBarBytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x) >> 1, npairs = static_cast<int>(gridDim.x) >> 1;
+  const int tiles_i2 = (p.M + 255) / 256;
+  const int ntiles = tiles_i2 * p.tiles_j;
+  const int kb_n = p.kblocks;
+  const int my_tiles = ntiles > pair ? (ntiles - pair + npairs - 1) / npairs : 0;
+  const int total = my_tiles * kb_n;  // K blocks this pair processes
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], kExpandWarps);
+    }
+    for (int s = 0; s < ES; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&exp_full[s], leader ? kExpandWarps + 1 : kExpandWarps);
+      mbar_init(&st_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 2 * kEpiWarps);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9 && lane == 0) tma_prefetch_desc(&tmA);
+  if (warp == 19 && lane == 0) tma_prefetch_desc(&tmQ);
+  if (warp == 8) {
+    tmem_alloc_pair(tmem_slot, C::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM of the pair allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t exp_full_ldr = dsmem_map(smem_u32(exp_full), 0);
+  const uint32_t tmem_empty_ldr = dsmem_map(smem_u32(tmem_empty), 0);
+  const uint32_t a_full_ldr = dsmem_map(smem_u32(a_full), 0);
+
+  if (warp == 9) {
+    // ------------------------------------------------ activation TMA (both CTAs, bytes to the leader)
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (; g < total; ++g) {
+        const int s = g % ES;
+        if (g >= ES && !mbar_wait_cluster(&st_empty[s], ((g / ES) & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int tile = pair + (g / kb_n) * npairs, kb = g % kb_n;
+        const int ti2 = tile % tiles_i2;
+        if (leader) mbar_arrive_expect_tx(&a_full[s], 2 * C::kAStage);
+        tma_load_2d_pair(stage_base + s * C::kStage, &tmA, a_full_ldr + static_cast<uint32_t>(s * 8), kb * 128,
+                         ti2 * 256 + static_cast<int>(rank) * 128);
+      }
+      if (!ok) {
+        // Loads already issued must land before the CTA can exit. The leader waits for the phases it
+        // armed; the peer, whose loads complete on the leader's barriers, waits out a fixed 100 us.
+        if (leader) {
+          for (int j = g > ES ? g - ES : 0; j < g; ++j) mbar_wait_cluster(&a_full[j % ES], (j / ES) & 1u, nullptr);
+        } else {
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 100000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 19) {
+    // ------------------------------------------------ packed weight TMA (both CTAs, own halves)
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (; g < total; ++g) {
+        const int rs = g % RS;
+        if (g >= RS && !mbar_wait(&raw_empty[rs], ((g / RS) & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int tile = pair + (g / kb_n) * npairs, kb = g % kb_n;
+        const int tj = tile / tiles_i2;
+        mbar_arrive_expect_tx(&raw_full[rs], C::kRawStage);
+        tma_load_2d(raw_base + rs * C::kRawStage, &tmQ, &raw_full[rs], kb * 64,
+                    tj * BN + static_cast<int>(rank) * 128);
+      }
+      if (!ok) {
+        for (int j = g > RS ? g - RS : 0; j < g; ++j) mbar_wait(&raw_full[j % RS], (j / RS) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 8 || warp == 18) {
+    // ------------------------------------------------ relays (peer): one cluster-scope arrival per K
+    // block on the leader's exp_full once the peer's 8 expansion warps have arrived locally; the two
+    // relay warps take alternate K blocks so the latencies of their release arrivals overlap.
+    if (!leader && lane == 0) {
+      const int r = warp == 8 ? 0 : 1;
+      for (int g = r; g < total; g += kPairRelays) {
+        const int s = g % ES;
+        if (!mbar_wait(&exp_full[s], (g / ES) & 1u, abort_flag)) break;
+        mbar_arrive_cluster(exp_full_ldr + static_cast<uint32_t>(s * 8));
+      }
+    }
+    // ------------------------------------------------ MMA issuer (leader only)
+    if (warp == 8 && leader && lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_i8(256, BN);
+      const uint32_t st_empty_peer = dsmem_map(smem_u32(st_empty), 1);
+      const uint32_t tmem_full_peer = dsmem_map(smem_u32(tmem_full), 1);
+      int g = 0, t = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < ntiles; tile += npairs, ++t) {
+        const int acc = t & 1, use = t >> 1;
+        if (use > 0 && !mbar_wait_cluster(&tmem_empty[acc], (use - 1) & 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kb_n; ++kb, ++g) {
+          const int s = g % ES;
+          const uint32_t par = (g / ES) & 1u;
+          if (!mbar_wait_cluster(&a_full[s], par, abort_flag) || !mbar_wait_cluster(&exp_full[s], par, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t aS = smem_u32(stage_base + s * C::kStage);
+          const uint64_t da = umma_desc_sw128(aS);
+          const uint64_t db = umma_desc_sw128(aS + C::kAStage);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_i8_ss_pair(d, da + 2 * kk, db + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_pair(smem_u32(&st_empty[s]));
+          umma_commit_pair(st_empty_peer + static_cast<uint32_t>(s * 8));
+        }
+        if (ok) {
+          umma_commit_pair(smem_u32(&tmem_full[acc]));
+          umma_commit_pair(tmem_full_peer + static_cast<uint32_t>(acc * 8));
+        }
+      }
+      umma_commit_pair(smem_u32(mma_done));
+      umma_commit_pair(dsmem_map(smem_u32(mma_done), 1));
+    }
+  } else if (warp >= 10) {
+    // ------------------------------------------------ weight int4 -> int8 expansion (both CTAs)
+    const int et = threadIdx.x - 10 * 32;
+    for (int g = 0; g < total; ++g) {
+      const int rs = g % RS, s = g % ES;
+      if (!mbar_wait(&raw_full[rs], (g / RS) & 1u, abort_flag) ||
+          (g >= ES && !mbar_wait_cluster(&st_empty[s], ((g / ES) & 1u) ^ 1u, abort_flag)))
+        break;
+      const uint8_t* src = raw_base + rs * C::kRawStage;
+      uint8_t* dst = stage_base + s * C::kStage + C::kAStage;
+      uint4 w[C::UPT];
+#pragma unroll
+      for (int i = 0; i < C::UPT; ++i) w[i] = *reinterpret_cast<const uint4*>(src + (et + i * kExpandThreads) * 16);
+#pragma unroll
+      for (int i = 0; i < C::UPT; ++i) {
+        const int u = et + i * kExpandThreads;
+        expand_chunk_natural(w[i], dst, u >> 2, u & 3);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&raw_empty[rs]);
+        mbar_arrive(&exp_full[s]);  // local; the peer's relays forward to the leader
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 0-7, both CTAs)
+    int t = 0;
+    for (int tile = pair; tile < ntiles; tile += npairs, ++t) {
+      const int acc_i = t & 1, use = t >> 1;
+      const int ti2 = tile % tiles_i2, tj = tile / tiles_i2;
+      const int ti = ti2 * 2 + static_cast<int>(rank);  // 128-row block of this CTA
+      epilogue_stage<BN>(p, tj, t & 1, est, threadIdx.x);
+      bool ok = mbar_wait_cluster(&tmem_full[acc_i], use & 1u, abort_flag);
+      ok = named_bar_and(1, kEpiThreads, ok && !*abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      epilogue_tile<BN, 4>(p, ti, tj, tmem_base + static_cast<uint32_t>(acc_i * BN), warp, lane, est, t & 1);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tmem_empty_ldr + static_cast<uint32_t>(acc_i * 8));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8 && lane == 0) mbar_wait_cluster(mma_done, 0, nullptr);  // the pair's MMAs into this CTA retired
+  __syncwarp();
+  cluster_sync();  // no CTA leaves while its peer may still address its shared memory
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::kTmemCols);
+  }
+}
+
 }  // namespace dscq

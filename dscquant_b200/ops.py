@@ -212,10 +212,11 @@ def w4a4_gemm(a: torch.Tensor, b: torch.Tensor, sx: torch.Tensor, sw: torch.Tens
 
 def w4a4_gemm_a8(a: torch.Tensor, b: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor, *, M: int | None = None,
                  N: int | None = None, bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
-                 out_dtype: torch.dtype = torch.bfloat16, return_raw: bool = False):
+                 out_dtype: torch.dtype = torch.bfloat16, return_raw: bool = False, variant: str = "auto"):
     """w4a4_gemm with int8 activation codes a [M, KP] (values in [-8, 7], e.g. rowquant(..., codes=True,
     packed_out=False)) and packed int4 weights b [N, KP/2]; symmetric activations only. Same bits as
-    w4a4_gemm on the packed form of a."""
+    w4a4_gemm on the packed form of a. `variant`: "auto" (CTA pairs for 256-wide tiles), "large_m"
+    (1-CTA kernel) or "large_m_pair" (CTA pairs)."""
     M = a.size(0) if M is None else M
     N = b.size(0) if N is None else N
     KP = b.size(1) * 2
@@ -227,8 +228,10 @@ def w4a4_gemm_a8(a: torch.Tensor, b: torch.Tensor, sx: torch.Tensor, sw: torch.T
     with torch.cuda.device(dev):
         out = torch.empty((M, N), dtype=out_dtype, device=dev)
         raw = torch.empty((M, N), dtype=torch.int32, device=dev) if return_raw else None
-        rc = _lib.load().dscq_matmul_a8(_ptr(a), a.stride(0), _ptr(b), _ptr(sx), _ptr(sw), _ptr(bias), _ptr(residual),
-                                        M, N, KP, _DT[out_dtype], _ptr(out), _ptr(raw), _stream(dev))
+        v = {"auto": _lib.GEMM_AUTO, "large_m": _lib.GEMM_LARGE_M, "large_m_pair": _lib.GEMM_LARGE_M_PAIR}[variant]
+        rc = _lib.load().dscq_matmul_a8_variant(_ptr(a), a.stride(0), _ptr(b), _ptr(sx), _ptr(sw), _ptr(bias),
+                                                _ptr(residual), M, N, KP, _DT[out_dtype], _ptr(out), _ptr(raw), v,
+                                                _stream(dev))
     _lib.check(rc, "matmul_a8")
     return (out, raw) if return_raw else out
 

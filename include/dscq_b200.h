@@ -140,6 +140,18 @@ int dscq_matmul_a8(const int8_t* a, int64_t ld_a, const uint8_t* b, const float*
                    void* stream);
 
 /*
+ * dscq_matmul_a8 with the kernel chosen by `variant` (no counterpart in the
+ * reference): DSCQ_GEMM_AUTO (what dscq_matmul_a8 does: CTA pairs with
+ * cta_group::2 MMAs for 256-wide tiles, the 1-CTA kernel otherwise),
+ * DSCQ_GEMM_LARGE_M (always the 1-CTA kernel) or DSCQ_GEMM_LARGE_M_PAIR
+ * (always CTA pairs). Same result bits for every variant; any other variant
+ * is DSCQ_ERR_INVALID.
+ */
+int dscq_matmul_a8_variant(const int8_t* a, int64_t ld_a, const uint8_t* b, const float* sx, const float* sw,
+                           const void* bias, const void* residual, int64_t M, int64_t N, int64_t KP, int out_dtype,
+                           void* out, int32_t* raw, int variant, void* stream);
+
+/*
  * Column-block form of dscq_matmul (no counterpart in the reference, which has
  * no multi-GPU code): the [M, N] result is written at rows 0..M-1, columns
  * col_off..col_off+N-1 of buffers with row stride ld_out elements, into each of

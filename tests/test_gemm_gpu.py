@@ -195,6 +195,31 @@ def test_gemm_a8_exact(oracle, cuda_device, M, N, KP):
     assert torch.equal(out, out_p)
 
 
+@pytest.mark.parametrize("M,N,KP", [(1, 128, 128), (130, 260, 192), (700, 300, 64), (1000, 2200, 448),
+                                    (4096, 2048, 1024), (2048, 4096, 4096), (260, 512, 11008)])
+def test_gemm_a8_variants_same_bits(oracle, cuda_device, M, N, KP):
+    """The 1-CTA A8 kernel and the CTA-pair A8 kernel (cta_group::2 MMAs, activation TMA completing on
+    the leader's barrier) give the oracle's int32 accumulators and identical outputs, on ragged M / N
+    / K and on shapes with several tiles per CTA pair."""
+    from dscquant_b200 import ops
+
+    rng = np.random.default_rng(M + 7 * N + KP)
+    codes = rng.integers(-8, 8, (M, KP)).astype(np.int8)
+    b = _packed(rng, N, KP)
+    sx = (rng.random(M, dtype=np.float32) * 0.1 + 1e-3).astype(np.float32)
+    sw = (rng.random(N, dtype=np.float32) * 0.01 + 1e-4).astype(np.float32)
+    T = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(cuda_device)  # noqa: E731
+    ref_raw = oracle.gemm_s4(oracle.pack_int4(codes), b, M, N, KP)
+    outs = {}
+    for v in ("large_m", "large_m_pair", "auto"):
+        out, raw = ops.w4a4_gemm_a8(T(codes), T(b), T(sx), T(sw), return_raw=True, variant=v)
+        np.testing.assert_array_equal(raw.cpu().numpy(), ref_raw, err_msg=v)
+        outs[v] = out
+    assert torch.equal(outs["large_m"], outs["large_m_pair"])
+    assert torch.equal(outs["large_m"], outs["auto"])
+    assert ops.device_status(cuda_device) == 0
+
+
 def test_gemm_a8_strided_codes_and_errors(oracle, cuda_device):
     """Codes with a padded row stride (a view into a wider buffer) and the argument checks."""
     from dscquant_b200 import ops
