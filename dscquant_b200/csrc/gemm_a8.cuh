@@ -241,14 +241,17 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
 // w4a4_gemm_pair, but with int8 activation codes: each CTA's 128 activation rows of a K block
 // arrive by a cta_group::2 TMA load whose bytes complete on the LEADER's a_full barrier, so the
 // activation half needs neither expansion nor a relayed arrival. Only the 128 weight rows of
-// each CTA are expanded (natural k order, 16 * code); the peer's expansion is forwarded to the
-// leader by two relay warps. Per K block and CTA the shared memory moves 16 KB (activation TMA)
+// each CTA are expanded (natural k order, 16 * code). The peer's relay thread forwards the
+// completion of its expansion with a 16-byte shared-to-shared bulk copy into the leader whose
+// bytes complete on the leader's exp_full: unlike a cluster-scope release arrival, which holds
+// the issuing thread ~0.7-1 us, the copy is issued without waiting, so one relay keeps up with
+// every K block. Per K block and CTA the shared memory moves 16 KB (activation TMA)
 // + 8 KB (weight TMA) + 8 KB read / 16 KB written by the expansion + 32 KB of MMA operand reads,
 // against 96 KB in the packed-activation pair kernel.
 //
-// Roles (640 threads): warps 0-7 epilogue; warp 8 MMA issuer (leader) or relay 0 (peer);
-// warp 9 activation TMA; warps 10-17 weight expansion; warp 18 relay 1 (peer); warp 19 weight TMA.
-constexpr int kPairA8Threads = 640;
+// Roles (608 threads): warps 0-7 epilogue; warp 8 MMA issuer (leader) or relay (peer); warp 9
+// activation TMA; warps 10-17 weight expansion; warp 18 weight TMA.
+constexpr int kPairA8Threads = 608;
 
 #ifndef DSCQ_PAIR_A8_ES
 #define DSCQ_PAIR_A8_ES 5
@@ -268,7 +271,9 @@ struct PairA8Cfg {
   static constexpr int kRawStage = 128 * 64;           // this CTA's 128 weight rows x 128 K (packed)
   static constexpr int UPT = 128 * 4 / kExpandThreads;  // 16-byte raw chunks per expansion thread
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kBarBytes = (2 * RS + 3 * ES + 5) * 8 + 16;
+  // barriers, TMEM slot and abort flag, then 16-byte signal slots: [ES] copy targets + 1 source
+  static constexpr int kSigOff = ((2 * RS + 3 * ES + 5) * 8 + 8 + 15) / 16 * 16;
+  static constexpr int kBarBytes = kSigOff + (ES + 1) * 16;
   static constexpr int kEpiBytes = static_cast<int>(sizeof(EpiStage<BN>));
   static constexpr int kSmemBytes = 1024 + ES * kStage + RS * kRawStage + kBarBytes + kEpiBytes;
   static_assert(ES >= 2 && RS >= 2, "need two stages of each ring");
@@ -290,13 +295,14 @@ __global__ void __launch_bounds__(kPairA8Threads, 1)
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = bars + RS;
   uint64_t* a_full = bars + 2 * RS;      // leader: one armed arrival + both CTAs' activation bytes
-  uint64_t* exp_full = a_full + ES;      // leader: 8 expansion warps + the relayed peer arrival; peer: 8
+  uint64_t* exp_full = a_full + ES;      // both: 8 expansion warps; leader: + 16 bytes copied by the peer
   uint64_t* st_empty = exp_full + ES;    // both: the leader's MMA commit
   uint64_t* tmem_full = st_empty + ES;   // [2] both: the leader's MMA commit
   uint64_t* tmem_empty = tmem_full + 2;  // [2] leader: 2 x 8 epilogue warps
   uint64_t* mma_done = tmem_full + 4;    // [1] both
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* sig = reinterpret_cast<uint8_t*>(bars) + C::kSigOff;  // [ES] copy targets, then the source
   EpiStage<BN>* est = reinterpret_cast<EpiStage<BN>*>(reinterpret_cast<uint8_t*>(bars) + C::kBarBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -316,7 +322,7 @@ __global__ void __launch_bounds__(kPairA8Threads, 1)
     }
     for (int s = 0; s < ES; ++s) {
       mbar_init(&a_full[s], 1);
-      mbar_init(&exp_full[s], leader ? kExpandWarps + 1 : kExpandWarps);
+      mbar_init(&exp_full[s], kExpandWarps);
       mbar_init(&st_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -328,7 +334,7 @@ __global__ void __launch_bounds__(kPairA8Threads, 1)
     fence_mbar_init();
   }
   if (warp == 9 && lane == 0) tma_prefetch_desc(&tmA);
-  if (warp == 19 && lane == 0) tma_prefetch_desc(&tmQ);
+  if (warp == 18 && lane == 0) tma_prefetch_desc(&tmQ);
   if (warp == 8) {
     tmem_alloc_pair(tmem_slot, C::kTmemCols);
     tmem_relinquish_pair();
@@ -341,6 +347,7 @@ __global__ void __launch_bounds__(kPairA8Threads, 1)
   const uint32_t exp_full_ldr = dsmem_map(smem_u32(exp_full), 0);
   const uint32_t tmem_empty_ldr = dsmem_map(smem_u32(tmem_empty), 0);
   const uint32_t a_full_ldr = dsmem_map(smem_u32(a_full), 0);
+  const uint32_t sig_ldr = dsmem_map(smem_u32(sig), 0);
 
   if (warp == 9) {
     // ------------------------------------------------ activation TMA (both CTAs, bytes to the leader)
@@ -371,7 +378,7 @@ __global__ void __launch_bounds__(kPairA8Threads, 1)
         }
       }
     }
-  } else if (warp == 19) {
+  } else if (warp == 18) {
     // ------------------------------------------------ packed weight TMA (both CTAs, own halves)
     if (lane == 0) {
       int g = 0;
@@ -392,20 +399,26 @@ __global__ void __launch_bounds__(kPairA8Threads, 1)
         for (int j = g > RS ? g - RS : 0; j < g; ++j) mbar_wait(&raw_full[j % RS], (j / RS) & 1u, nullptr);
       }
     }
-  } else if (warp == 8 || warp == 18) {
-    // ------------------------------------------------ relays (peer): one cluster-scope arrival per K
-    // block on the leader's exp_full once the peer's 8 expansion warps have arrived locally; the two
-    // relay warps take alternate K blocks so the latencies of their release arrivals overlap.
+  } else if (warp == 8) {
+    // ------------------------------------------------ relay (peer): once the peer's 8 expansion warps
+    // have arrived locally for a K block, a 16-byte bulk copy into the leader completes on the
+    // leader's exp_full of that stage (armed with expect_tx by the leader's first expansion warp).
     if (!leader && lane == 0) {
-      const int r = warp == 8 ? 0 : 1;
-      for (int g = r; g < total; g += kPairRelays) {
+      int g = 0;
+      for (; g < total; ++g) {
         const int s = g % ES;
         if (!mbar_wait(&exp_full[s], (g / ES) & 1u, abort_flag)) break;
-        mbar_arrive_cluster(exp_full_ldr + static_cast<uint32_t>(s * 8));
+        bulk_copy_to_peer(sig_ldr + static_cast<uint32_t>(s * 16), sig + ES * 16, 16,
+                          exp_full_ldr + static_cast<uint32_t>(s * 8));
+      }
+      if (g < total) {  // aborted: copies already issued land within microseconds
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 100000ull) {
+        }
       }
     }
     // ------------------------------------------------ MMA issuer (leader only)
-    if (warp == 8 && leader && lane == 0) {
+    if (leader && lane == 0) {
       constexpr uint32_t idesc = umma_idesc_i8(256, BN);
       const uint32_t st_empty_peer = dsmem_map(smem_u32(st_empty), 1);
       const uint32_t tmem_full_peer = dsmem_map(smem_u32(tmem_full), 1);
@@ -463,7 +476,10 @@ __global__ void __launch_bounds__(kPairA8Threads, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&raw_empty[rs]);
-        mbar_arrive(&exp_full[s]);  // local; the peer's relays forward to the leader
+        if (leader && warp == 10)
+          mbar_arrive_expect_tx(&exp_full[s], 16);  // + the 16 bytes the peer's relay copies in
+        else
+          mbar_arrive(&exp_full[s]);
       }
     }
   } else {

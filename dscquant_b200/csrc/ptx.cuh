@@ -304,6 +304,17 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "l"(map), "r"(bar_cluster_addr), "r"(x), "r"(y)
       : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16, 16-byte aligned ends) from this CTA's
+// shared memory to `dst_cluster` in another CTA of the cluster; the bytes
+// complete on the mbarrier `bar_cluster` of that CTA. The issuing thread does not
+// wait, so a CTA can signal a peer's barrier without a blocking remote arrival.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, const void* src, uint32_t bytes,
+                                                  uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster),
+               "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
+               : "memory");
+}
 // Arrive (release at cluster scope) on an mbarrier given by a shared::cluster address.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
