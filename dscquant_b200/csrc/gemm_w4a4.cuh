@@ -190,8 +190,7 @@ __device__ __forceinline__ void epilogue16(const GemmParams& p, int ti, int tj, 
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kPersistThreads = 576;  // 8 epilogue + 2 control + 8 expansion warps
-constexpr int kPairThreads = 608;     // + one more relay warp (pair kernel)
-constexpr int kPairRelays = 2;        // peer warps forwarding stage arrivals to the leader
+constexpr int kPairThreads = 576;     // pair kernel: same roles, warp 8 is the peer's relay
 
 template <int BN>
 struct EpiStage {
@@ -676,12 +675,15 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
 // [128r, 128r+128) x all 256 columns of the accumulator. Per SM this halves
 // the B-operand bytes that TMA writes, the expansion reads and writes, and
 // the tensor cores read from shared memory, for the same MMA throughput.
-// Only the leader (rank 0) issues MMAs. Both CTAs' expansion warps arrive on
-// the leader's `exp_full` (the peer through its cluster address); the
-// leader's commits arrive on `exp_empty`, `tmem_full` and `mma_done` of both
-// CTAs; both CTAs' epilogue warps arrive on the leader's `tmem_empty`.
-//   warps 0-3 epilogue, warp 4 TMEM allocator (+ MMA issuer in the leader),
-//   warp 5 TMA producer, warps 6-13 expansion.
+// Only the leader (rank 0) issues MMAs. Each CTA's expansion warps arrive on
+// their own `exp_full`; the peer's relay thread then issues a 16-byte bulk
+// copy into the leader whose bytes complete on the leader's `exp_full` of the
+// same stage (armed by the leader's first expansion warp), so the leader
+// learns of both halves without a blocking remote arrival. The leader's
+// commits arrive on `exp_empty`, `tmem_full` and `mma_done` of both CTAs; both
+// CTAs' epilogue warps arrive on the leader's `tmem_empty`.
+//   warps 0-7 epilogue, warp 8 TMEM allocator + MMA issuer (leader) or relay
+//   (peer), warp 9 TMA producer, warps 10-17 expansion (576 threads).
 struct PairCfg {
   static constexpr int BN = 256;                    // pair tile N (128 B rows per CTA)
   static constexpr int kRows = 256;                 // 128 A rows + 128 B rows per CTA
@@ -694,7 +696,9 @@ struct PairCfg {
   static constexpr int RS = (212 * 1024 - ES * kExpStage - static_cast<int>(sizeof(EpiStage<256>))) / kRawStage;
   static constexpr int UPT = kRows * 4 / kExpandThreads;
   static constexpr int kTmemCols = 2 * BN;          // two accumulators x 256 columns
-  static constexpr int kBarBytes = (2 * RS + 2 * ES + 5) * 8 + 16;
+  // barriers, TMEM slot and abort flag, then 16-byte signal slots: [ES] copy targets + 1 source
+  static constexpr int kSigOff = ((2 * RS + 2 * ES + 5) * 8 + 8 + 15) / 16 * 16;
+  static constexpr int kBarBytes = kSigOff + (ES + 1) * 16;
   static constexpr int kEpiBytes = static_cast<int>(sizeof(EpiStage<BN>));
   static constexpr int kSmemBytes = 1024 + ES * kExpStage + RS * kRawStage + kBarBytes + kEpiBytes;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -712,13 +716,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(raw_base + RS * C::kRawStage);
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = bars + RS;
-  uint64_t* exp_full = bars + 2 * RS;            // leader: 2 x 8 expansion warps
+  uint64_t* exp_full = bars + 2 * RS;            // both: 8 expansion warps; leader: + 16 bytes from the peer
   uint64_t* exp_empty = bars + 2 * RS + ES;      // both: leader's MMA commit
   uint64_t* tmem_full = bars + 2 * RS + 2 * ES;  // [2] both: leader's MMA commit
   uint64_t* tmem_empty = tmem_full + 2;          // [2] leader: 2 x 4 epilogue warps
   uint64_t* mma_done = tmem_full + 4;            // [1] both
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* sig = reinterpret_cast<uint8_t*>(bars) + C::kSigOff;  // [ES] copy targets, then the source
   EpiStage<BN>* est = reinterpret_cast<EpiStage<BN>*>(reinterpret_cast<uint8_t*>(bars) + C::kBarBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -735,8 +740,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_init(&raw_empty[s], kExpandWarps);
     }
     for (int s = 0; s < ES; ++s) {
-      // leader: its 8 expansion warps + one relayed arrival for the peer's 8; peer: its own 8
-      mbar_init(&exp_full[s], leader ? kExpandWarps + 1 : kExpandWarps);
+      // 8 expansion warps; on the leader the first one also arms 16 bytes for the peer's signal
+      mbar_init(&exp_full[s], kExpandWarps);
       mbar_init(&exp_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -763,6 +768,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   // leader's barriers as seen from this CTA (cluster addresses)
   const uint32_t exp_full_ldr = dsmem_map(smem_u32(exp_full), 0);
   const uint32_t tmem_empty_ldr = dsmem_map(smem_u32(tmem_empty), 0);
+  const uint32_t sig_ldr = dsmem_map(smem_u32(sig), 0);
 
   if (warp == 9) {
     // ------------------------------------------------ TMA producer (both CTAs, own halves)
@@ -787,22 +793,28 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         for (int j = g > RS ? g - RS : 0; j < g; ++j) mbar_wait(&raw_full[j % RS], (j / RS) & 1u, nullptr);
       }
     }
-  } else if (warp == 8 || warp == 18) {
-    // ------------------------------------------------ relays (peer): one cluster-scope arrival per
-    // stage on the leader once the peer's 8 expansion warps have arrived locally. A release
-    // arrival at cluster scope holds its thread for a while, so kPairRelays warps (8 and 18) take
-    // alternate K blocks and their latencies overlap.
+  } else if (warp == 8) {
+    // ------------------------------------------------ relay (peer): once the peer's 8 expansion warps
+    // have arrived locally for a K block, a 16-byte bulk copy into the leader completes on the
+    // leader's exp_full of that stage. The copy is issued without waiting (a cluster-scope release
+    // arrival would hold this thread ~0.7-1 us per K block).
     if (!leader && lane == 0) {
-      const int r = warp == 8 ? 0 : 1;
       const int total = (ntiles > pair ? (ntiles - pair + npairs - 1) / npairs : 0) * kb_n;
-      for (int g = r; g < total; g += kPairRelays) {
+      int g = 0;
+      for (; g < total; ++g) {
         const int s = g % ES;
         if (!mbar_wait(&exp_full[s], (g / ES) & 1u, abort_flag)) break;
-        mbar_arrive_cluster(exp_full_ldr + static_cast<uint32_t>(s * 8));
+        bulk_copy_to_peer(sig_ldr + static_cast<uint32_t>(s * 16), sig + ES * 16, 16,
+                          exp_full_ldr + static_cast<uint32_t>(s * 8));
+      }
+      if (g < total) {  // aborted: copies already issued land within microseconds
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 100000ull) {
+        }
       }
     }
     // ------------------------------------------------ MMA issuer (leader only)
-    if (warp == 8 && leader && lane == 0) {
+    if (leader && lane == 0) {
       constexpr uint32_t idesc = umma_idesc_i8(256, BN);
       const uint32_t exp_empty_peer = dsmem_map(smem_u32(exp_empty), 1);
       const uint32_t tmem_full_peer = dsmem_map(smem_u32(tmem_full), 1);
@@ -868,7 +880,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&raw_empty[rs]);
-          mbar_arrive(&exp_full[es]);  // local; the peer's relay forwards to the leader
+          if (leader && warp == 10)
+            mbar_arrive_expect_tx(&exp_full[es], 16);  // + the 16 bytes the peer's relay copies in
+          else
+            mbar_arrive(&exp_full[es]);
         }
       }
     }
