@@ -50,6 +50,9 @@ def parse():
     p.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"])
     p.add_argument("--tokens", type=int, default=2048)
     p.add_argument("--replicas", type=int, default=4, help="layer replicas cycled so the working set exceeds L2")
+    p.add_argument("--activations", default="packed", choices=["packed", "int8"],
+                   help="activation codes handed from the quantizer to the GEMM: packed nibbles (dscq_matmul, "
+                        "the reference's format) or one int8 code per element (dscq_matmul_a8); same result bits")
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--kernel-case", choices=["gemm", "quant"], default=None,
@@ -421,6 +424,7 @@ def main():
         reps.append((mods, xs))
     outs = {name: torch.empty((M, N), dtype=torch.bfloat16, device=dev) for name, _, N in LAYER}
 
+    a8 = args.activations == "int8"
     stream = torch.cuda.current_stream(dev)
     gemm_events = []  # (start, end, ops) of GEMM launches in the timed region
     quant_events = []  # (start, end, bytes)
@@ -432,11 +436,11 @@ def main():
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-            qs[key] = ops.rowquant(xs[key], "act_sym", rotate=True, KP=K)
+            qs[key] = ops.rowquant(xs[key], "act_sym", rotate=True, KP=K, codes=a8, packed_out=not a8)
             if record:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record(stream)
-                quant_events.append((e0, e1, M * K * 2 + M * K // 2 + 4 * M))
+                quant_events.append((e0, e1, M * K * 2 + (M * K if a8 else M * K // 2) + 4 * M))
         for name, K, N in LAYER:
             ql = mods[name]
             q = qs[INPUT_OF[name]]
@@ -444,9 +448,14 @@ def main():
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-            rc = _lib.load().dscq_matmul(ops._ptr(q.packed), ops._ptr(p["packed"]), ops._ptr(q.scales), None,
-                                         ops._ptr(p["sw"]), None, None, None, M, N, K, _lib.BF16,
-                                         ops._ptr(outs[name]), None, 0, ops._stream(dev))
+            if a8:
+                rc = _lib.load().dscq_matmul_a8(ops._ptr(q.codes), K, ops._ptr(p["packed"]), ops._ptr(q.scales),
+                                                ops._ptr(p["sw"]), None, None, M, N, K, _lib.BF16,
+                                                ops._ptr(outs[name]), None, ops._stream(dev))
+            else:
+                rc = _lib.load().dscq_matmul(ops._ptr(q.packed), ops._ptr(p["packed"]), ops._ptr(q.scales), None,
+                                             ops._ptr(p["sw"]), None, None, None, M, N, K, _lib.BF16,
+                                             ops._ptr(outs[name]), None, 0, ops._stream(dev))
             _lib.check(rc, "matmul")
             if record:
                 e1 = torch.cuda.Event(enable_timing=True)
@@ -505,6 +514,8 @@ def main():
     from dscquant_b200.hostio import HostPipeline
 
     pipe = HostPipeline(dev)
+    for name, _, _ in LAYER:
+        mods[name].int8_activations = a8  # same activation format as the device-resident step
     e2e_mods = [mods[name] for name, _, _ in LAYER]
     e2e_in = [host_in[name] for name, _, _ in LAYER]
     e2e_out = [host_out[name] for name, _, _ in LAYER]
@@ -586,10 +597,11 @@ def main():
                "sample": f"{rows} tokens x 7 layer linears per step, {n} steps, oracle C W4A4 linear "
                          "(rotation, symmetric int4 codes, int32 GEMM, epilogue) with pthreads"}
 
-    # DRAM bytes per w4a4_gemm_pair launch from one ncu capture of each benchmark shape at M = 2048
+    # DRAM bytes per GEMM launch from one ncu capture of each benchmark shape at M = 2048
     # (dram__bytes_read.sum + dram__bytes_write.sum), launch-weighted over the step's 7 GEMMs
+    gemm_kernel = "w4a4_gemm_pair_a8" if a8 else "w4a4_gemm_pair"
     traffic = None
-    if M == 2048:
+    if M == 2048 and not a8:
         per_shape = {(4096, 4096): 12.662e6, (4096, 11008): 26.866e6, (11008, 4096): 33.891e6}
         traffic = sum(per_shape[(k, n)] for _, k, n in LAYER) / len(LAYER)
 
@@ -602,12 +614,13 @@ def main():
             "config": {"workload": "llama2-7b-layer-linears", "tokens_per_gpu": M,
                        "shapes_KxN": [[k, n] for _, k, n in LAYER], "rotation": "WHT-4096 / H172xH64 (K=11008)",
                        "activation_quant": "symmetric per-token int4", "weight_quant": "symmetric per-channel int4",
+                       "activation_codes": "int8 (one code per byte)" if a8 else "packed int4 nibbles",
                        "parallelism": f"dp{world} over tokens" if world > 1 else "single GPU",
                        "l2": f"{R} layer replicas cycled (working set > 126 MB L2)"},
             "gpu_launches": 11 * args.steps,
-            "roofline": {"kernel": "w4a4_gemm_pair", "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
+            "roofline": {"kernel": gemm_kernel, "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
                          "unit": "TFLOP/s", "frac": gemm_tops / int8_peak, "traffic": traffic,
-                         "traffic_note": "w4a4_gemm_pair bytes per launch, ncu capture of each shape at M=2048 (profiles/)",
+                         "traffic_note": f"{gemm_kernel} bytes per launch, ncu capture of each shape at M=2048 (profiles/)",
                          "peak_note": f"int8 dense = 2 x {peaks['source']} bf16 cuBLAS {peaks['bf16_tflops']} TFLOP/s; "
                                       "ops are integer ops (2 per MAC)",
                          "share_of_step": gemm_ms / elapsed_ms},

@@ -172,7 +172,12 @@ cudaError_t launch_wht(const dscq::RowQuantParams& p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(dscq::wht_quant_pow2<LOGK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM);
   if (e != cudaSuccess) return e;
-  const unsigned grid = static_cast<unsigned>((p.rows_out + C::ROWS - 1) / C::ROWS);
+  // persistent: as many CTAs as are resident at once (each walks row groups with a one-group prefetch)
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dscq::wht_quant_pow2<LOGK>, C::THREADS, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const int64_t groups = (p.rows_out + C::ROWS - 1) / C::ROWS;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(groups, std::max(per_sm, 1) * num_sms()));
   dscq::wht_quant_pow2<LOGK><<<grid, C::THREADS, C::SMEM, st>>>(p);
   return cudaGetLastError();
 }
@@ -198,7 +203,7 @@ cudaError_t launch_rotq(const CUtensorMap& tm, const dscq::RotqParams& rp, cudaS
   const int grid = std::min(rp.groups, num_sms());
   const int nwarps = std::max(rp.tma_warp, rp.mma_warp) + 1;
   const int threads = std::max(nwarps, (rp.nteam - 1) * rp.team_stride + rp.tw) * 32;
-  if (threads > dscq::RqThreads<MT>::value) return cudaErrorInvalidConfiguration;
+  if (threads > dscq::RqThreads<MT, G>::value) return cudaErrorInvalidConfiguration;
   dscq::rotq_tc<MT, G><<<grid, threads, smem, st>>>(tm, rp);
   return cudaGetLastError();
 }
@@ -431,8 +436,8 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
     return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize needs a rotation with K = a' * 64 (a' <= 224), a "
                                       "symmetric mode, bf16 input, KP == K and 16-byte aligned rows");
   // AUTO: the tcgen05 kernel has a longer fixed prologue (TMEM, Hadamard operand) and wins once
-  // there is enough work: from 4096 rows, or from 1024 rows when the dense factor is larger than 64
-  const bool tc_auto = ap_tc >= 32 && (rows_out >= 4096 || (ap_tc > 64 && rows_out >= 1024));
+  // there is enough work: from 2048 rows, or from 1024 rows when the dense factor is larger than 64
+  const bool tc_auto = ap_tc >= 32 && (rows_out >= 2048 || (ap_tc > 64 && rows_out >= 1024));
   if (tc_ok && (variant == DSCQ_QUANT_TC || (variant == DSCQ_QUANT_AUTO && tc_auto))) {
     dscq::RotqParams rp;
     rp.p = p;
@@ -449,16 +454,17 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
     rp.a_bytes = static_cast<uint32_t>(rp.mt * rp.nkb * 16384);
     rp.stage_bytes = static_cast<uint32_t>(rp.P * rp.ap16 * 128);
     rp.ns = std::min<int>(dscq::kRqMaxStages, (210 * 1024 - static_cast<int>(rp.a_bytes)) / static_cast<int>(rp.stage_bytes));
-    // one MMA spans G token blocks: G = 4 (N = 256) with one M tile, 2 (N = 128) with two; the
-    // stage ring holds whole groups
-    const int G = rp.mt == 1 ? 4 : 2;
+    // one MMA spans G = 2 token blocks (N = 128); the stage ring holds whole groups. The epilogue
+    // (TMEM load, 64-point WHT, absmax, codes) is the longest role, so one M tile runs four teams,
+    // one per TMEM slot of 128 columns
+    const int G = 2;
     rp.ns = rp.ns / G * G;
-    if (rp.mt == 1) {  // two teams of four warps (lane quadrants 0-3), then the TMA and MMA warps
+    if (rp.mt == 1) {  // four teams of four warps (lane quadrants 0-3), then the TMA and MMA warps
       rp.tw = 4;
       rp.team_stride = 4;
-      rp.nteam = 2;
-      rp.tma_warp = 8;
-      rp.mma_warp = 9;
+      rp.nteam = 4;
+      rp.tma_warp = 16;
+      rp.mma_warp = 17;
     } else {  // two teams of 4 + ceil((a' - 128) / 32) warps at warps 0.. and 8..
       rp.tw = 4 + (rp.ap - 128 + 31) / 32;
       rp.team_stride = 8;
@@ -471,7 +477,7 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
     CUtensorMap tm;
     st = make_rows_map(&tm, x, M, rp.ap, ld_x, rp.ap16, rp.P);
     if (st) return st;
-    cudaError_t e = rp.mt == 1 ? launch_rotq<1, 4>(tm, rp, cst) : launch_rotq<2, 2>(tm, rp, cst);
+    cudaError_t e = rp.mt == 1 ? launch_rotq<1, 2>(tm, rp, cst) : launch_rotq<2, 2>(tm, rp, cst);
     if (e != cudaSuccess) return cuda_fail(e, "launch rotq_tc");
     return DSCQ_OK;
   }

@@ -160,15 +160,16 @@ __device__ __forceinline__ int quant_row64(const float2 (&u)[32], float cm, floa
   return sums ? quant_store64<true, CLAMP>(u, cm, lo, prow, crow) : quant_store64<false, CLAMP>(u, cm, lo, prow, crow);
 }
 
-// Threads per CTA: 10 warps for one M tile (two teams of 4 + TMA + MMA), up to 16 for two
+// Threads per CTA: one M tile with G = 4: 10 warps (two teams of 4 + TMA + MMA); one M tile with
+// G = 2: 18 warps (four teams of 4 + TMA + MMA, one TMEM slot per team); two M tiles: up to 16
 // (two teams of up to 7 for a' <= 224, TMA, MMA).
-template <int MT>
+template <int MT, int G>
 struct RqThreads {
-  static constexpr int value = MT == 1 ? 320 : 512;
+  static constexpr int value = MT == 1 ? (G == 2 ? 576 : 320) : 512;
 };
 
 template <int MT, int G>
-__global__ void __launch_bounds__(RqThreads<MT>::value, 1)
+__global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
     rotq_tc(const __grid_constant__ CUtensorMap tmX, const RotqParams rp) {
   const RowQuantParams& p = rp.p;
   extern __shared__ uint8_t rq_smem_dyn[];
@@ -232,28 +233,55 @@ __global__ void __launch_bounds__(RqThreads<MT>::value, 1)
   if (builder) {
     // ---- H_a^T staged in shared memory: ht[c * a + r] = H_a[r][c], so 8 consecutive k of one
     // A row are 8 consecutive bytes.
+    // 16-byte loads, up to 8 in flight per thread before any store (a dependent byte load per
+    // entry would leave each thread waiting out the global latency a*a/nb times).
     const int8_t* ht = nullptr;
     if (rp.a_base > 1) {
       const int a = rp.a_base;
-      for (int i = bt; i < a * a; i += nb) {
+      const int total = a * a;
+      const int nvec = (reinterpret_cast<uintptr_t>(p.h_a) & 15u) == 0 ? total / 16 : 0;
+      for (int v0 = bt; v0 < nvec; v0 += 8 * nb) {
+        int4 buf[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int v = v0 + k * nb;
+          buf[k] = v < nvec ? __ldg(reinterpret_cast<const int4*>(p.h_a) + v) : make_int4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int v = v0 + k * nb;
+          if (v >= nvec) break;
+          int r = (16 * v) / a, c = 16 * v - r * a;
+          const int8_t* e = reinterpret_cast<const int8_t*>(&buf[k]);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            stage_h[c * a + r] = static_cast<uint8_t>(e[j]);
+            if (++c == a) {
+              c = 0;
+              ++r;
+            }
+          }
+        }
+      }
+      for (int i = nvec * 16 + bt; i < total; i += nb) {
         const int r = i / a, c = i - r * a;
         stage_h[c * a + r] = static_cast<uint8_t>(p.h_a[i]);
       }
       ht = reinterpret_cast<const int8_t*>(stage_h);
     }
     named_bar_sync(5, nb);
-    // ---- A = H'^T (K-major, 128-byte swizzle). Chunk u = (row << 5) | (kb << 3) | ch holds
+    // ---- A = H'^T (K-major, 128-byte swizzle). Chunk u = (row * nkb + kb) * 8 + ch holds
     // A[row][k0 .. k0+7], k0 = kb * 64 + ch * 8, row = m * 128 + r; A[i'][i] = H'[i][i'].
     {
-      const int chunks = MT * 128 * 32;
+      const int nkb = rp.nkb;
+      const int chunks = MT * 128 * nkb * 8;
       const int s = rp.s_log, a = rp.a_base, msk = (1 << s) - 1;
       for (int u = bt; u < chunks; u += nb) {
-        const int ch = u & 7, kb = (u >> 3) & 3, row = u >> 5;
-        if (kb >= rp.nkb) continue;
+        const int ch = u & 7, rk = u >> 3;
+        const int row = rk / nkb, kb = rk - row * nkb;
         const int k0 = kb * 64 + ch * 8;
         int ip, ikb;  // i' of the row and i of k0 inside the token block
         bool row_live;
-        uint32_t klive = 0xFFu;  // live k of the chunk (bit j: k0 + j)
         if (MT == 1 && P > 1) {
           const int sh = rp.log2_ap16;
           ip = row & (ap16 - 1);
@@ -264,17 +292,31 @@ __global__ void __launch_bounds__(RqThreads<MT>::value, 1)
           ikb = k0;
           row_live = ip < ap;
         }
-        for (int j = 0; j < 8; ++j)
-          if (ikb + j >= ap) klive &= ~(1u << j);
+        // live k of the chunk (bit j: ikb + j < a')
+        uint32_t klive = !row_live ? 0u : (ikb + 8 <= ap ? 0xFFu : (ikb >= ap ? 0u : (1u << (ap - ikb)) - 1u));
         uint32_t neg = 0;  // bit j: H'[ikb + j][ip] < 0
-        if (row_live && klive) {
-          for (int j = 0; j < 8; ++j) neg |= static_cast<uint32_t>(__popc((ikb + j) & ip & msk) & 1) << j;
-          if (a > 1) {
-            for (int j = 0; j < 8; ++j)
-              if (ikb + j < ap) neg ^= static_cast<uint32_t>(ht[(ip >> s) * a + ((ikb + j) >> s)] < 0) << j;
+        if (klive) {
+          // Sylvester factor: ikb is a multiple of 8, so (ikb + j) & ip splits into the bits of ikb and
+          // of j: sign = parity(ikb & ip) ^ parity(j & ip & 7), the latter an 8-bit Walsh row
+          const uint32_t m7 = static_cast<uint32_t>(ip & msk & 7);
+          neg = static_cast<uint32_t>((0x963C5AF066CCAA00ull >> (8 * m7)) & 0xFFu);
+          if (__popc(ikb & ip & msk) & 1) neg ^= 0xFFu;
+          if (a > 1) {  // dense factor H_a[(ikb + j) >> s][ip >> s], read from the transposed copy ht
+            const int8_t* hrow = ht + (ip >> s) * a;
+            if (s >= 3) {  // one entry covers the 8 k of the chunk
+              if (hrow[ikb >> s] < 0) neg ^= 0xFFu;
+            } else if (s == 0 && (a & 3) == 0) {  // 8 consecutive entries, two aligned words
+              const uint32_t w0 = *reinterpret_cast<const uint32_t*>(hrow + ikb);
+              const uint32_t w1 = *reinterpret_cast<const uint32_t*>(hrow + ikb + 4);
+              const uint32_t s0 = ((w0 >> 7) & 1u) | ((w0 >> 14) & 2u) | ((w0 >> 21) & 4u) | ((w0 >> 28) & 8u);
+              const uint32_t s1 = ((w1 >> 7) & 1u) | ((w1 >> 14) & 2u) | ((w1 >> 21) & 4u) | ((w1 >> 28) & 8u);
+              neg ^= s0 | (s1 << 4);
+            } else {
+              for (int j = 0; j < 8; ++j)
+                if (ikb + j < ap) neg ^= static_cast<uint32_t>(hrow[(ikb + j) >> s] < 0) << j;
+            }
           }
         }
-        if (!row_live) klive = 0;
         uint32_t wv[4];
   #pragma unroll
         for (int t = 0; t < 4; ++t) {
@@ -283,7 +325,7 @@ __global__ void __launch_bounds__(RqThreads<MT>::value, 1)
           wv[t] = lo | (hi << 16);
         }
         const int m = row >> 7, r = row & 127;
-        uint8_t* dst = a_base + (m * rp.nkb + kb) * 16384 + r * 128 + ((ch ^ (r & 7)) << 4);
+        uint8_t* dst = a_base + (m * nkb + kb) * 16384 + r * 128 + ((ch ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
       }
     }
