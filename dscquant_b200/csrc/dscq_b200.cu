@@ -172,12 +172,7 @@ cudaError_t launch_wht(const dscq::RowQuantParams& p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(dscq::wht_quant_pow2<LOGK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM);
   if (e != cudaSuccess) return e;
-  // persistent: as many CTAs as are resident at once (each walks row groups with a one-group prefetch)
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dscq::wht_quant_pow2<LOGK>, C::THREADS, C::SMEM);
-  if (e != cudaSuccess) return e;
-  const int64_t groups = (p.rows_out + C::ROWS - 1) / C::ROWS;
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(groups, std::max(per_sm, 1) * num_sms()));
+  const unsigned grid = static_cast<unsigned>((p.rows_out + C::ROWS - 1) / C::ROWS);
   dscq::wht_quant_pow2<LOGK><<<grid, C::THREADS, C::SMEM, st>>>(p);
   return cudaGetLastError();
 }

@@ -14,11 +14,6 @@
 //            magic add, nibbles of adjacent columns packed into bytes and
 //            stored as 16-bit words (coalesced across the row's threads)
 //
-// Persistent: the grid holds as many CTAs as fit on the SMs; each CTA walks its
-// row groups and issues the 16-byte loads of its next group into registers
-// before it processes the current one, so a launch keeps (nearly) all of a
-// small problem's rows in flight from the start and a large one streams.
-//
 // Same definitions as the general kernel (rowquant.cuh): y = x H_K / sqrt(K),
 // scale = max(absmax(y)*clip/7, 1e-8), code = clamp(rn(y/scale)) to [-8, 7]
 // (activations) or [-7, 7] (weights). The float order differs from a float64
@@ -53,19 +48,7 @@ __device__ __forceinline__ float2 bf16x2_to_f2(uint32_t w) {
 }
 
 template <int LOGK>
-__device__ __forceinline__ void wht_load_row(const RowQuantParams& p, int row, int t,
-                                             uint4 (&buf)[WhtCfg<LOGK>::E / 8]) {
-  constexpr int E = WhtCfg<LOGK>::E;
-  const bool live = row < p.M;
-  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) +
-                                                    static_cast<int64_t>(live ? row : 0) * p.ld_x) +
-                     t * (E / 8);
-#pragma unroll
-  for (int q = 0; q < E / 8; ++q) buf[q] = live ? __ldcs(src + q) : make_uint4(0, 0, 0, 0);
-}
-
-template <int LOGK>
-__global__ void __launch_bounds__(128, 2) wht_quant_pow2(const RowQuantParams p) {
+__global__ void __launch_bounds__(128) wht_quant_pow2(const RowQuantParams p) {
   using C = WhtCfg<LOGK>;
   constexpr int E = C::E, TR = C::TR, G = C::G, GPT = C::GPT, K = C::K;
   constexpr int CM = E / 4 - 1;  // chunk swizzle mask
@@ -76,29 +59,25 @@ __global__ void __launch_bounds__(128, 2) wht_quant_pow2(const RowQuantParams p)
 
   const int r_local = threadIdx.x / TR;
   const int t = threadIdx.x % TR;
-  float* sb = sbase + r_local * K;
-  const int ngroups = (p.rows_out + C::ROWS - 1) / C::ROWS;
-
-  uint4 nxt[E / 8];
-  if (static_cast<int>(blockIdx.x) < ngroups) wht_load_row<LOGK>(p, blockIdx.x * C::ROWS + r_local, t, nxt);
-
-  for (int grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {  // uniform across the CTA
-  const int row = grp * C::ROWS + r_local;
+  const int row = blockIdx.x * C::ROWS + r_local;
+  const bool live = row < p.M;
   const bool active = row < p.rows_out;
-  uint4 cur[E / 8];
-#pragma unroll
-  for (int q = 0; q < E / 8; ++q) cur[q] = nxt[q];
-  if (grp + static_cast<int>(gridDim.x) < ngroups)
-    wht_load_row<LOGK>(p, (grp + gridDim.x) * C::ROWS + r_local, t, nxt);
+  float* sb = sbase + r_local * K;
 
   // ---------------- phase 1: contiguous E elements, butterflies over bits [0, LE)
   float2 V[E / 2];
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) +
+                                                      static_cast<int64_t>(live ? row : 0) * p.ld_x) +
+                       t * (E / 8);
 #pragma unroll
-  for (int q = 0; q < E / 8; ++q) {
-    V[4 * q + 0] = bf16x2_to_f2(cur[q].x);
-    V[4 * q + 1] = bf16x2_to_f2(cur[q].y);
-    V[4 * q + 2] = bf16x2_to_f2(cur[q].z);
-    V[4 * q + 3] = bf16x2_to_f2(cur[q].w);
+    for (int q = 0; q < E / 8; ++q) {
+      const uint4 w = live ? __ldcs(src + q) : make_uint4(0, 0, 0, 0);
+      V[4 * q + 0] = bf16x2_to_f2(w.x);
+      V[4 * q + 1] = bf16x2_to_f2(w.y);
+      V[4 * q + 2] = bf16x2_to_f2(w.z);
+      V[4 * q + 3] = bf16x2_to_f2(w.w);
+    }
   }
 #pragma unroll
   for (int m = 0; m < E / 2; ++m) V[m] = make_float2(V[m].x + V[m].y, V[m].x - V[m].y);
@@ -215,8 +194,6 @@ __global__ void __launch_bounds__(128, 2) wht_quant_pow2(const RowQuantParams p)
       csum = s_sum[r_local][0] + s_sum[r_local][1];
     }
     if (t == 0 && active) p.row_sums[row] = csum;
-  }
-  __syncthreads();  // the next group reuses the shared-memory rows and reduction slots
   }
 }
 
