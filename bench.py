@@ -505,11 +505,12 @@ def main():
 
     # ---- e2e through the public API (QuantLinear.forward) with pinned host buffers
     mods = reps[0][0]
-    host_in = {name: torch.empty((M, K), dtype=torch.bfloat16, pin_memory=True) for name, K, _ in LAYER}
+    # one pinned host input per distinct layer input (q/k/v share one, gate/up another), copied once
+    host_in = {key: torch.empty((M, K), dtype=torch.bfloat16, pin_memory=True) for key, K in INPUT_K.items()}
     host_out = {name: torch.empty((M, N), dtype=torch.bfloat16, pin_memory=True) for name, _, N in LAYER}
-    for name, K, _ in LAYER:
-        host_in[name].copy_(reps[0][1][INPUT_OF[name]].cpu())
-    h2d = sum(M * K * 2 for _, K, _ in LAYER)
+    for key in INPUT_K:
+        host_in[key].copy_(reps[0][1][key].cpu())
+    h2d = sum(M * K * 2 for K in INPUT_K.values())
     d2h = sum(M * N * 2 for _, _, N in LAYER)
     from dscquant_b200.hostio import HostPipeline
 
@@ -517,7 +518,7 @@ def main():
     for name, _, _ in LAYER:
         mods[name].int8_activations = a8  # same activation format as the device-resident step
     e2e_mods = [mods[name] for name, _, _ in LAYER]
-    e2e_in = [host_in[name] for name, _, _ in LAYER]
+    e2e_in = [host_in[INPUT_OF[name]] for name, _, _ in LAYER]
     e2e_out = [host_out[name] for name, _, _ in LAYER]
 
     def e2e_step():

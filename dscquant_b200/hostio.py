@@ -16,7 +16,9 @@ respect to the host and to the caller's stream; the returned event (also
 `done_event`) completes when every host output of the call is written:
 `synchronize()` waits for it on the host, `stream.wait_event(ev)` on a stream.
 Host inputs must stay unchanged and host outputs unread until then (the
-copies are asynchronous).
+copies are asynchronous). A host tensor passed as the input of several modules
+of one call (the shared input of a layer's q/k/v or gate/up projections) is
+copied to the device once; its buffer is released after its last consumer.
 
 The reference has no counterpart (its QuantLinear works on device tensors
 only); this is the host-memory entry point of the same W4A4 path.
@@ -60,14 +62,21 @@ class HostPipeline:
         start.record(torch.cuda.current_stream(self.device))
         self.s_in.wait_event(start)
         self.s_comp.wait_event(start)
+        seen: dict[int, tuple[int, torch.cuda.Event]] = {}  # id(host input) -> (buffer, loaded event)
         for i, (mod, hin, hout) in enumerate(zip(modules, host_inputs, host_outputs)):
-            dbuf = self._buffer(i, hin)
-            with torch.cuda.stream(self.s_in):
-                if i in self._free:
-                    self.s_in.wait_event(self._free[i])
-                dbuf.copy_(hin, non_blocking=True)
-                loaded = torch.cuda.Event()
-                loaded.record(self.s_in)
+            if id(hin) in seen:  # same host tensor as an earlier module of this call: no second copy
+                j, loaded = seen[id(hin)]
+                dbuf = self._bufs[j]
+            else:
+                j = i
+                dbuf = self._buffer(i, hin)
+                with torch.cuda.stream(self.s_in):
+                    if i in self._free:
+                        self.s_in.wait_event(self._free[i])
+                    dbuf.copy_(hin, non_blocking=True)
+                    loaded = torch.cuda.Event()
+                    loaded.record(self.s_in)
+                seen[id(hin)] = (j, loaded)
             with torch.cuda.stream(self.s_comp):
                 self.s_comp.wait_event(loaded)
                 y = mod(dbuf)
@@ -75,7 +84,7 @@ class HostPipeline:
                     raise ValueError(f"host output {i} must be {tuple(y.shape)} {y.dtype}")
                 computed = torch.cuda.Event()
                 computed.record(self.s_comp)
-                self._free[i] = computed
+                self._free[j] = computed  # the compute stream is in order: the last consumer frees j
             with torch.cuda.stream(self.s_out):
                 self.s_out.wait_event(computed)
                 hout.copy_(y, non_blocking=True)

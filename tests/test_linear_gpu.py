@@ -182,6 +182,34 @@ def test_host_pipeline_matches_forward(cuda_device):
         pipe.run(mods, [t.clone() for t in h_in], h_out)  # not pinned
 
 
+def test_host_pipeline_shared_input(cuda_device):
+    """A host input shared by several modules (q/k/v style) is copied once and still gives every
+    module's forward bits, over repeated calls that reuse the device buffers."""
+    from dscquant_b200 import QuantConfig, QuantLinear
+    from dscquant_b200.hostio import HostPipeline
+
+    K = 4096
+    x = torch.randn(80, K, device=cuda_device, dtype=torch.bfloat16)
+    x2 = torch.randn(80, K, device=cuda_device, dtype=torch.bfloat16)
+    h_x, h_x2 = x.cpu().pin_memory(), x2.cpu().pin_memory()
+    mods, h_in, h_out, refs = [], [], [], []
+    for i, (N, src, hsrc) in enumerate([(512, x, h_x), (256, x, h_x), (768, x2, h_x2), (256, x, h_x)]):
+        ql = QuantLinear(_linear(synthetic.weights_bf16(N, K, seed=60 + i), None, cuda_device), QuantConfig())
+        ql.enabled = True
+        refs.append(ql(src).cpu())
+        mods.append(ql)
+        h_in.append(hsrc)
+        h_out.append(torch.empty((80, N), dtype=torch.bfloat16).pin_memory())
+    pipe = HostPipeline(cuda_device)
+    for _ in range(3):
+        for h in h_out:
+            h.zero_()
+        pipe.run(mods, h_in, h_out)
+        pipe.synchronize()
+        for h, r in zip(h_out, refs):
+            assert torch.equal(h, r)
+
+
 def test_int8_activation_path_same_bits(cuda_device):
     """QuantLinear with int8_activations (A8 GEMM above 64 tokens) returns the packed path's bits."""
     from dscquant_b200 import QuantConfig, QuantLinear
