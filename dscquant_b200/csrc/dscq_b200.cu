@@ -449,11 +449,12 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
     rp.a_bytes = static_cast<uint32_t>(rp.mt * rp.nkb * 16384);
     rp.stage_bytes = static_cast<uint32_t>(rp.P * rp.ap16 * 128);
     rp.ns = std::min<int>(dscq::kRqMaxStages, (210 * 1024 - static_cast<int>(rp.a_bytes)) / static_cast<int>(rp.stage_bytes));
-    // one MMA spans G = 2 token blocks (N = 128); the stage ring holds whole groups. The epilogue
-    // (TMEM load, 64-point WHT, absmax, codes) is the longest role, so one M tile runs four teams,
-    // one per TMEM slot of 128 columns
-    const int G = 2;
+    // one MMA spans G token blocks: G = 4 (N = 256) with one M tile, 2 (N = 128) with two; the
+    // stage ring holds whole groups. The epilogue (TMEM load, 64-point WHT, absmax, codes) is the
+    // longest role: with one M tile four teams split each group's four blocks
+    const int G = rp.mt == 1 ? 4 : 2;
     rp.ns = rp.ns / G * G;
+    rp.split = rp.mt == 1 ? 1 : 0;
     if (rp.mt == 1) {  // four teams of four warps (lane quadrants 0-3), then the TMA and MMA warps
       rp.tw = 4;
       rp.team_stride = 4;
@@ -472,7 +473,7 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
     CUtensorMap tm;
     st = make_rows_map(&tm, x, M, rp.ap, ld_x, rp.ap16, rp.P);
     if (st) return st;
-    cudaError_t e = rp.mt == 1 ? launch_rotq<1, 2>(tm, rp, cst) : launch_rotq<2, 2>(tm, rp, cst);
+    cudaError_t e = rp.mt == 1 ? launch_rotq<1, 4>(tm, rp, cst) : launch_rotq<2, 2>(tm, rp, cst);
     if (e != cudaSuccess) return cuda_fail(e, "launch rotq_tc");
     return DSCQ_OK;
   }

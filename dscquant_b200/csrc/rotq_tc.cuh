@@ -57,6 +57,7 @@ struct RotqParams {
   int tw;                // warps per team
   int team_stride;       // team t owns warps [t * team_stride, t * team_stride + tw)
   int tma_warp, mma_warp;
+  int split;             // 1: every team takes one block of each MMA group; 0: teams take whole groups
 };
 
 // 64 consecutive TMEM columns of this thread's lane as 32 float2 (natural column order).
@@ -160,12 +161,12 @@ __device__ __forceinline__ int quant_row64(const float2 (&u)[32], float cm, floa
   return sums ? quant_store64<true, CLAMP>(u, cm, lo, prow, crow) : quant_store64<false, CLAMP>(u, cm, lo, prow, crow);
 }
 
-// Threads per CTA: one M tile with G = 4: 10 warps (two teams of 4 + TMA + MMA); one M tile with
-// G = 2: 18 warps (four teams of 4 + TMA + MMA, one TMEM slot per team); two M tiles: up to 16
-// (two teams of up to 7 for a' <= 224, TMA, MMA).
+// Threads per CTA: one M tile: 18 warps (four teams of 4 that split each group of G = 4 blocks,
+// TMA, MMA); two M tiles: up to 16 (two teams of up to 7 for a' <= 224 taking whole groups of
+// G = 2 blocks, TMA, MMA).
 template <int MT, int G>
 struct RqThreads {
-  static constexpr int value = MT == 1 ? (G == 2 ? 576 : 320) : 512;
+  static constexpr int value = MT == 1 ? 576 : 512;
 };
 
 template <int MT, int G>
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
     }
     for (int s = 0; s < S; ++s) {
       mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], tw);
+      mbar_init(&tempty[s], rp.split ? tw * rp.nteam : tw);
     }
     mbar_init(done, 1);
     mbar_init(aready, 1);
@@ -414,21 +415,32 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
                                     static_cast<int>(gridDim.x)
                               : 0;
     int it = 0;
-    for (int q = team; q * G < my_blocks; q += rp.nteam) {
+    // split: all teams walk every group and team t takes block t of it (the group's TMEM slot is
+    // freed once every team has loaded its block); otherwise team t takes groups t, t + nteam, ...
+    const int q0 = rp.split ? 0 : team, qstep = rp.split ? 1 : rp.nteam;
+    for (int q = q0; q * G < my_blocks; q += qstep) {
       const int slot = q % S, use = q / S, n0 = q * G;
       const int nblk = min(G, my_blocks - n0);
       bool ok = mbar_wait(&tfull[slot], use & 1u, abort_flag);
       ok = named_bar_and(bar_id, bar_cnt, ok && !*abort_flag);
       if (!ok) break;
       tc_fence_after();
-      for (int b = 0; b < nblk; ++b, ++it) {
+      const int b_lo = rp.split ? team : 0;
+      const int b_hi = rp.split ? min(team + 1, nblk) : nblk;
+      if (b_lo >= b_hi) {  // no block of this group for this team: release the slot right away
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[slot]);
+        continue;
+      }
+      for (int b = b_lo; b < b_hi; ++b, ++it) {
         const int g = blockIdx.x + (n0 + b) * gridDim.x;  // token block
         const int par = it & 1;
         float2 v[32];
         tmem_ld64(tmem_base + (static_cast<uint32_t>(qd * 32) << 16) +
                       static_cast<uint32_t>(slot * SLOT + mtile * 64 * G + b * 64),
                   v);
-        if (b == nblk - 1) {
+        if (b == b_hi - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[slot]);  // the group's columns may be overwritten
