@@ -62,8 +62,8 @@ def parse():
     p.add_argument("--N", type=int, default=11008)
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--variant", type=int, default=0,
-                   help="--kernel-case gemm: dscq_matmul variant 0-5, or dscq_matmul_a8 (int8 activation codes): "
-                        "6 = AUTO (CTA pairs), 7 = the 1-CTA kernel")
+                   help="--kernel-case gemm: dscq_matmul variant 0-6, or dscq_matmul_a8 (int8 activation codes): "
+                        "7 = AUTO (CTA pairs), 8 = the 1-CTA kernel")
     p.add_argument("--qvariant", default="auto", choices=["auto", "tc", "legacy"],
                    help="rotate+quantize kernel for --kernel-case quant")
     p.add_argument("--graph", action="store_true",
@@ -128,7 +128,7 @@ def kernel_case(args) -> None:
     else:
         w = bf(synthetic.weights_bf16(args.N, args.K, seed=2))
         qw = ops.rowquant(w, "weight_sym", rotate=True, KP=args.K)
-        qx = ops.rowquant(x, "act_sym", rotate=True, KP=args.K, codes=args.variant in (6, 7))
+        qx = ops.rowquant(x, "act_sym", rotate=True, KP=args.K, codes=args.variant in (7, 8))
         out = torch.empty((args.M, args.N), dtype=torch.bfloat16, device=dev)
         from dscquant_b200 import _lib
 
@@ -139,8 +139,8 @@ def kernel_case(args) -> None:
         lib = _lib.load()
 
         def fn(i=0):
-            if args.variant in (6, 7):  # int8 activation codes: AUTO (CTA pairs) / the 1-CTA kernel
-                v = _lib.GEMM_AUTO if args.variant == 6 else _lib.GEMM_LARGE_M
+            if args.variant in (7, 8):  # int8 activation codes: AUTO (CTA pairs) / the 1-CTA kernel
+                v = _lib.GEMM_AUTO if args.variant == 7 else _lib.GEMM_LARGE_M
                 _lib.check(lib.dscq_matmul_a8_variant(ops._ptr(qx.codes), args.K, ops._ptr(wcopies[i % copies]),
                                                       ops._ptr(qx.scales), ops._ptr(qw.scales), None, None, args.M,
                                                       args.N, args.K, _lib.BF16, ops._ptr(out), None, v,

@@ -17,6 +17,7 @@ DSCQ_OK, DSCQ_ERR_INVALID, DSCQ_ERR_CUDA, DSCQ_ERR_UNSUPPORTED, DSCQ_ERR_RANGE =
 BF16, F16, F32 = 0, 1, 2
 ACT_SYM, WEIGHT_SYM, ACT_ASYM, ACT_ASYM_TORCH = 0, 1, 2, 3
 GEMM_AUTO, GEMM_SMALL_M, GEMM_LARGE_M, GEMM_LARGE_M_DIRECT, GEMM_LARGE_M_PAIR, GEMM_SMALL_M_TC = 0, 1, 2, 3, 4, 5
+GEMM_LARGE_M_PAIR_TMEM = 6
 QUANT_AUTO, QUANT_TC, QUANT_LEGACY = 0, 1, 2
 
 _i32, _i64, _u32p, _f32, _vp, _cp = (ctypes.c_int, ctypes.c_int64, ctypes.POINTER(ctypes.c_uint32), ctypes.c_float,

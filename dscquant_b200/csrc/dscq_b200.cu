@@ -18,6 +18,7 @@
 #include "kron_quant.cuh"
 #include "gemv_w4a4.cuh"
 #include "gemm_a8.cuh"
+#include "gemm_pair_tm.cuh"
 #include "rotq_tc.cuh"
 
 namespace {
@@ -93,6 +94,22 @@ int make_u8_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, 
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return DSCQ_OK;
+}
+
+// As make_u8_map with the 64-byte swizzle (16-byte chunk c of box row r lands at chunk
+// c ^ ((r >> 1) & 3)), so that one thread per row reads shared memory without bank conflicts.
+int make_u8_map_sw64(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled (64B swizzle) failed (" + std::to_string(r) + ")");
   return DSCQ_OK;
 }
 
@@ -293,6 +310,31 @@ int launch_gemm_pair_a8(const CUtensorMap& tmA, const CUtensorMap& tmQ, const ds
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, kern, tmA, tmQ, gp);
   if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_pair_a8");
+  return DSCQ_OK;
+}
+
+int launch_gemm_pair_tm(const CUtensorMap& tmA, const CUtensorMap& tmB, const dscq::GemmParams& gp,
+                        cudaStream_t stream) {
+  using C = dscq::PairTmCfg;
+  auto kern = dscq::w4a4_gemm_pair_tm;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a4_gemm_pair_tm)");
+  const int tiles = ((gp.M + 255) / 256) * gp.tiles_j;
+  const int pairs = std::min(tiles, num_sms() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(dscq::kPairThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, gp);
+  if (e != cudaSuccess) return cuda_fail(e, "launch w4a4_gemm_pair_tm");
   return DSCQ_OK;
 }
 
@@ -542,7 +584,7 @@ static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, cons
   DSCQ_REQUIRE(!zx || sums, "asymmetric activations (zx) need weight code sums");
   DSCQ_REQUIRE(out_dtype == DSCQ_BF16 || out_dtype == DSCQ_F16 || out_dtype == DSCQ_F32, "out_dtype must be bf16/f16/f32");
   DSCQ_REQUIRE(aligned(a, 16) && aligned(b, 16), "packed operands must be 16-byte aligned");
-  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_SMALL_M_TC, "unknown GEMM variant");
+  DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_LARGE_M_PAIR_TMEM, "unknown GEMM variant");
   int st = check_device(nullptr);
   if (st) return st;
 
@@ -573,6 +615,10 @@ static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, cons
     } else {
       BN = (t256 >= nsm / 2 && eff(t256) + 0.1 >= eff(t128)) ? 256 : 128;
     }
+    if (variant == DSCQ_GEMM_LARGE_M_PAIR_TMEM) {  // 256 x 192 pair tiles, activations in TMEM
+      BN = 192;
+      splits = 1;
+    }
     tj = (N + BN - 1) / BN;
     persistent = splits == 1;
   }
@@ -583,12 +629,13 @@ static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, cons
   const uint8_t* P = swap ? b : a;
   const uint8_t* Q = swap ? a : b;
   const int64_t rowsP = swap ? N : M, rowsQ = swap ? M : N;
-  st = make_u8_map(&tmP, P, rowsP, kbytes, kbytes, 128);
+  const bool pair_tm = variant == DSCQ_GEMM_LARGE_M_PAIR_TMEM;
+  st = pair_tm ? make_u8_map_sw64(&tmP, P, rowsP, kbytes, kbytes, 128) : make_u8_map(&tmP, P, rowsP, kbytes, kbytes, 128);
   if (st) return st;
   // AUTO takes the CTA-pair kernel whenever the 256-wide tile is chosen (2-SM MMAs); LARGE_M keeps
   // the 1-CTA persistent kernel for A/B timing
   const bool pair = persistent && BN == 256 && (variant == DSCQ_GEMM_LARGE_M_PAIR || variant == DSCQ_GEMM_AUTO);
-  st = make_u8_map(&tmQ, Q, rowsQ, kbytes, kbytes, pair ? 128 : BN);
+  st = make_u8_map(&tmQ, Q, rowsQ, kbytes, kbytes, pair_tm ? dscq::PairTmCfg::kBRows : (pair ? 128 : BN));
   if (st) return st;
 
   dscq::GemmParams gp;
@@ -626,6 +673,7 @@ static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, cons
     gp.Q = b;  // weights
     return launch_gemv(gp, s);
   }
+  if (pair_tm) return launch_gemm_pair_tm(tmP, tmQ, gp, s);
   if (pair) return launch_gemm_pair(tmP, tmQ, gp, s);
   if (persistent && variant == DSCQ_GEMM_LARGE_M_DIRECT)
     return BN == 256 ? launch_gemm_ldg<256>(gp, s) : launch_gemm_ldg<128>(gp, s);

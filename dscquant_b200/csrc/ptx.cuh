@@ -286,6 +286,29 @@ __device__ __forceinline__ void umma_i8_ss_pair(uint32_t d_tmem, uint64_t adesc,
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// cta_group::2 int8 MMA whose A operand comes from tensor memory: each CTA of
+// the pair holds its 128 rows of A in its own TMEM at column address `a_tmem`
+// (one lane per row, 4 consecutive k per 32-bit column), B from shared memory.
+__device__ __forceinline__ void umma_i8_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 16 consecutive TMEM columns of this warp's 32 lanes from 16 registers per thread (thread i ->
+// lane base + i). tcgen05.st is asynchronous: tmem_st_wait() before signalling the consumer.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Arrive once on the mbarrier at `bar_cluster_addr` (this CTA's or the peer's,
 // a shared::cluster address) when all prior cta_group::2 MMAs of this thread complete.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {

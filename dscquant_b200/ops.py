@@ -203,7 +203,7 @@ def w4a4_gemm(a: torch.Tensor, b: torch.Tensor, sx: torch.Tensor, sw: torch.Tens
         raw = torch.empty((M, N), dtype=torch.int32, device=dev) if return_raw else None
         v = {"auto": _lib.GEMM_AUTO, "small_m": _lib.GEMM_SMALL_M, "large_m": _lib.GEMM_LARGE_M,
              "large_m_direct": _lib.GEMM_LARGE_M_DIRECT, "large_m_pair": _lib.GEMM_LARGE_M_PAIR,
-             "small_m_tc": _lib.GEMM_SMALL_M_TC}[variant]
+             "small_m_tc": _lib.GEMM_SMALL_M_TC, "large_m_pair_tmem": _lib.GEMM_LARGE_M_PAIR_TMEM}[variant]
         rc = _lib.load().dscq_matmul(_ptr(a), _ptr(b), _ptr(sx), _ptr(zx), _ptr(sw), _ptr(sums), _ptr(bias),
                                      _ptr(residual), M, N, KP, _DT[out_dtype], _ptr(out), _ptr(raw), v, _stream(dev))
     _lib.check(rc, "w4a4_gemm")

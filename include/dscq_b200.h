@@ -45,6 +45,7 @@ extern "C" {
 #define DSCQ_GEMM_LARGE_M_DIRECT 3 /* as LARGE_M, operands loaded to registers (A/B timing) */
 #define DSCQ_GEMM_LARGE_M_PAIR 4   /* 256x256 tiles on CTA pairs (cta_group::2); AUTO's choice for large M */
 #define DSCQ_GEMM_SMALL_M_TC 5     /* tcgen05 with weights on the 128-row MMA side (tokens as MMA N) */
+#define DSCQ_GEMM_LARGE_M_PAIR_TMEM 6 /* 256x192 tiles on CTA pairs, expanded activations in TMEM */
 
 /* Rotate+quantize kernel choice (dscq_rowquant_variant `variant`) */
 #define DSCQ_QUANT_AUTO 0

@@ -74,15 +74,15 @@ def test_gemm_exact_forced_variant(oracle, cuda_device, variant, M, N, KP):
     _run(oracle, cuda_device, M, N, KP, variant=variant)
 
 
-@pytest.mark.parametrize("variant", ["large_m", "large_m_direct", "large_m_pair"])
+@pytest.mark.parametrize("variant", ["large_m", "large_m_direct", "large_m_pair", "large_m_pair_tmem"])
 @pytest.mark.parametrize("M,N,KP", [(1024, 2304, 1024), (1000, 2200, 448), (2048, 4096, 256), (384, 5120, 4096),
-                                    (1300, 4400, 640)])
+                                    (1300, 4400, 640), (130, 200, 192), (4096, 2112, 1024)])
 def test_gemm_exact_persistent_variants(oracle, cuda_device, variant, M, N, KP):
     """Shapes with enough tiles for the persistent kernels (TMA-staged and direct-load), incl. ragged edges."""
     _run(oracle, cuda_device, M, N, KP, variant=variant)
 
 
-@pytest.mark.parametrize("variant", ["large_m", "large_m_direct", "large_m_pair"])
+@pytest.mark.parametrize("variant", ["large_m", "large_m_direct", "large_m_pair", "large_m_pair_tmem"])
 def test_gemm_persistent_epilogue_options(oracle, cuda_device, variant):
     _run(oracle, cuda_device, 640, 2304, 512, variant=variant, asym=True, bias=True, residual=True)
 
