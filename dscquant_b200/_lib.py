@@ -35,6 +35,8 @@ SIGNATURES = {
                              _vp, _vp, _vp, _i64, _vp]),
     "dscq_rowquant_variant": (_i32, [_vp, _i32, _i64, _i64, _i64, _i32, _i32, _vp, _i32, _f32, _i64, _i64, _vp,
                                      _i64, _vp, _vp, _vp, _vp, _i64, _i32, _vp]),
+    "dscq_rowquant_headrot": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _i32, _f32, _i64, _i64, _vp, _i64, _vp,
+                                     _vp, _i64, _vp]),
     "dscq_matmul": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i32, _vp]),
     "dscq_matmul_a8": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp]),
     "dscq_matmul_a8_variant": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i32,

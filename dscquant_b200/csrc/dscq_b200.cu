@@ -19,6 +19,7 @@
 #include "gemv_w4a4.cuh"
 #include "gemm_a8.cuh"
 #include "gemm_pair_tm.cuh"
+#include "headrot_quant.cuh"
 #include "rotq_tc.cuh"
 
 namespace {
@@ -110,6 +111,22 @@ int make_u8_map_sw64(CUtensorMap* map, const void* base, int64_t rows, int64_t c
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled (64B swizzle) failed (" + std::to_string(r) + ")");
+  return DSCQ_OK;
+}
+
+// bf16 matrix [rows, cols] (row stride ld elements) in boxes of 128 rows x 64 columns landing with
+// the 128-byte swizzle: the K-major UMMA operand layout.
+int make_bf16_sw128_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2u};
+  cuuint32_t box[2] = {64u, 128u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DSCQ_ERR_CUDA, "cuTensorMapEncodeTiled (bf16) failed (" + std::to_string(r) + ")");
   return DSCQ_OK;
 }
 
@@ -400,6 +417,72 @@ int dscq_rotation_split(int64_t K, int* a, int* b) {
     return fail(DSCQ_ERR_UNSUPPORTED, "K=" + std::to_string(K) + " has no supported Hadamard split");
   *a = aa;
   *b = 1 << lb;
+  return DSCQ_OK;
+}
+
+int dscq_rowquant_headrot(const void* x, int64_t M, int64_t K, int64_t ld_x, int heads, const void* rot_hi,
+                          const void* rot_lo, int mode, float clip, int64_t rows_out, int64_t KP, uint8_t* packed,
+                          int64_t ld_packed, float* scales, int8_t* codes, int64_t ld_codes, void* stream) {
+  DSCQ_REQUIRE(x && rot_hi && rot_lo && scales, "x, rot_hi, rot_lo and scales must not be null");
+  DSCQ_REQUIRE(packed || codes, "need packed or codes output");
+  DSCQ_REQUIRE(heads >= 4 && heads % 4 == 0 && heads / 4 <= dscq::kHrMaxCluster && K == 128 * heads,
+               "head rotation needs K = 128 * heads with heads a multiple of 4, at most 64");
+  DSCQ_REQUIRE(M >= 1 && rows_out >= M && rows_out <= (int64_t(1) << 30) && KP == K, "invalid rows / KP");
+  DSCQ_REQUIRE(mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM, "head rotation supports the symmetric modes");
+  DSCQ_REQUIRE(clip > 0.f && clip <= 1.f, "clip must be in (0, 1]");
+  DSCQ_REQUIRE(ld_x >= K && ld_x % 8 == 0 && aligned(x, 16) && aligned(rot_hi, 16) && aligned(rot_lo, 16),
+               "x needs 16-byte aligned rows (ld_x a multiple of 8), rotations 16-byte aligned");
+  DSCQ_REQUIRE(!packed || (ld_packed >= K / 2 && ld_packed % 16 == 0 && aligned(packed, 16)),
+               "packed rows must be 16-byte aligned");
+  DSCQ_REQUIRE(!codes || (ld_codes >= K && ld_codes % 16 == 0 && aligned(codes, 16)), "codes rows must be 16-byte aligned");
+  int st = check_device(nullptr);
+  if (st) return st;
+  dscq::HeadRotParams hp{};
+  dscq::RowQuantParams& p = hp.p;
+  p.x = x;
+  p.x_dtype = DSCQ_BF16;
+  p.M = M;
+  p.K = K;
+  p.ld_x = ld_x;
+  p.mode = mode;
+  p.clip = clip;
+  p.norm = 1.f;
+  p.rows_out = rows_out;
+  p.KP = KP;
+  p.packed = packed;
+  p.ld_packed = ld_packed;
+  p.scales = scales;
+  p.codes = codes;
+  p.ld_codes = ld_codes;
+  hp.heads = heads;
+  hp.cluster = heads / 4;
+  CUtensorMap tmX, tmHi, tmLo;
+  if ((st = make_bf16_sw128_map(&tmX, x, M, K, ld_x))) return st;
+  if ((st = make_bf16_sw128_map(&tmHi, rot_hi, static_cast<int64_t>(heads) * 128, 128, 128))) return st;
+  if ((st = make_bf16_sw128_map(&tmLo, rot_lo, static_cast<int64_t>(heads) * 128, 128, 128))) return st;
+  auto kern = dscq::headrot_quant;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dscq::kHrSmem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(headrot_quant)");
+  if (hp.cluster > 8) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(non-portable cluster)");
+  }
+  const int64_t tiles = (rows_out + 127) / 128;
+  DSCQ_REQUIRE(tiles * hp.cluster < (int64_t(1) << 31), "problem too large");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * hp.cluster));
+  cfg.blockDim = dim3(dscq::kHrThreads);
+  cfg.dynamicSmemBytes = dscq::kHrSmem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(hp.cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, tmX, tmHi, tmLo, hp);
+  if (e != cudaSuccess) return cuda_fail(e, "launch headrot_quant");
   return DSCQ_OK;
 }
 

@@ -183,6 +183,45 @@ def rowquant(x: torch.Tensor, mode: str = "act_sym", clip: float = 1.0, rotate: 
     return RowQuant(packed, scales, zeros, sums, cds, KP)
 
 
+def head_rotation_operands(R: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-head rotation matrices R [heads, 128, 128] (fp32, e.g. core/transforms.py Rotation.matrices())
+    -> the (hi, lo) bf16 operands of rowquant_headrot: hi + lo ~ R to ~2^-17, each stored transposed per
+    head (op[h][e][d] = R[h][d][e]). Call once per set of matrices."""
+    if R.dim() != 3 or R.shape[1:] != (128, 128):
+        raise ValueError("R must be [heads, 128, 128]")
+    if not R.is_cuda:
+        raise RuntimeError("R must be a CUDA tensor")
+    Rt = R.detach().float().transpose(1, 2).contiguous()
+    hi = Rt.to(torch.bfloat16)
+    lo = (Rt - hi.float()).to(torch.bfloat16)
+    return hi.contiguous(), lo.contiguous()
+
+
+def rowquant_headrot(x: torch.Tensor, hi: torch.Tensor, lo: torch.Tensor, mode: str = "act_sym", clip: float = 1.0,
+                     rows_out: int | None = None, codes: bool = False, packed_out: bool = True) -> RowQuant:
+    """Online per-head block rotation (y = x blockdiag(R_h)) fused with symmetric per-row int4 quantisation,
+    one tcgen05 kernel (include/dscq_b200.h, dscq_rowquant_headrot). x [M, 128 * heads] bf16; hi, lo from
+    head_rotation_operands."""
+    if not x.is_cuda or x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise RuntimeError("rowquant_headrot expects a 2-D bf16 CUDA tensor with unit column stride")
+    M, K = x.shape
+    heads = hi.shape[0]
+    if K != 128 * heads or hi.shape != lo.shape:
+        raise ValueError("x must have 128 * heads columns")
+    rows_out = M if rows_out is None else rows_out
+    m = _MODES[mode]
+    dev = x.device
+    with torch.cuda.device(dev):
+        packed = torch.empty((rows_out, K // 2), dtype=torch.uint8, device=dev) if packed_out else None
+        scales = torch.empty((rows_out,), dtype=torch.float32, device=dev)
+        cds = torch.empty((rows_out, K), dtype=torch.int8, device=dev) if codes else None
+        rc = _lib.load().dscq_rowquant_headrot(_ptr(x), M, K, x.stride(0), heads, _ptr(hi), _ptr(lo), m, float(clip),
+                                               rows_out, K, _ptr(packed), K // 2 if packed_out else 0, _ptr(scales),
+                                               _ptr(cds), K if codes else 0, _stream(dev))
+    _lib.check(rc, "rowquant_headrot")
+    return RowQuant(packed, scales, None, None, cds, K)
+
+
 def w4a4_gemm(a: torch.Tensor, b: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor, *, M: int | None = None,
               N: int | None = None, zx: torch.Tensor | None = None, sums: torch.Tensor | None = None,
               bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,

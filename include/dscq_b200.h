@@ -111,6 +111,24 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
                           int64_t ld_codes, int variant, void* stream);
 
 /*
+ * Online per-head block rotation + symmetric per-row int4 quantisation: the
+ * online form of the reference's Rotation transform (core/transforms.py:51-52,
+ * absorbed into the v / o weights by core/linear.py:28-37; the reference has no
+ * online form). x [M, ld_x] bf16 with K = 128 * heads (heads a multiple of 4, at
+ * most 64), rotated per head, y[t, 128h + e] = sum_d x[t, 128h + d] R_h[d][e],
+ * then quantised per row exactly like dscq_rowquant in DSCQ_ACT_SYM /
+ * DSCQ_WEIGHT_SYM mode (scale = max(absmax * clip / 7, 1e-8)). R_h is given as
+ * two bf16 parts, rot_hi + rot_lo ~ R_h (lo = the bf16 rounding of R_h - hi),
+ * each [heads, 128, 128] stored transposed per head: rot[h][e][d] = R_h[d][e].
+ * Outputs as dscq_rowquant: packed [rows_out, KP/2] (or NULL), scales
+ * [rows_out], codes [rows_out, ld_codes] (or NULL); no zero points or code
+ * sums. KP must equal K; rows M .. rows_out-1 are zero rows.
+ */
+int dscq_rowquant_headrot(const void* x, int64_t M, int64_t K, int64_t ld_x, int heads, const void* rot_hi,
+                          const void* rot_lo, int mode, float clip, int64_t rows_out, int64_t KP, uint8_t* packed,
+                          int64_t ld_packed, float* scales, int8_t* codes, int64_t ld_codes, void* stream);
+
+/*
  * Replaces matmul_cuda(a, b, sx, zx, sw, sums, bias, M, N, fused,
  * force_decode, fp32), kernel/w4a4.cu:189-225.
  *   a [>= M rows, KP/2] u8 packed activations (row stride KP/2 bytes)
