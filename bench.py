@@ -55,7 +55,7 @@ def parse():
                         "the reference's format) or one int8 code per element (dscq_matmul_a8); same result bits")
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    p.add_argument("--kernel-case", choices=["gemm", "quant"], default=None,
+    p.add_argument("--kernel-case", choices=["gemm", "quant", "headrot"], default=None,
                    help="run REPS launches of one kernel on [M, K] x [N, K] (for profilers) and exit")
     p.add_argument("--M", type=int, default=8192)
     p.add_argument("--K", type=int, default=4096)
@@ -111,7 +111,23 @@ def kernel_case(args) -> None:
     dev = torch.device("cuda", 0)
     bf = lambda b: torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16).to(dev)  # noqa: E731
     x = bf(synthetic.activations_bf16(args.M, args.K, seed=1))
-    if args.kernel_case == "quant":
+    if args.kernel_case == "headrot":  # online per-head rotation + quantisation, heads = K / 128
+        import torch as _t
+        g = _t.Generator().manual_seed(5)
+        a = _t.randn(args.K // 128, 128, 128, generator=g, dtype=_t.float64) * 0.05
+        hi, lo = ops.head_rotation_operands(_t.matrix_exp(a - a.transpose(1, 2)).float().to(dev))
+        units = args.M * args.K * 2.5 + 4 * args.M
+        copies = max(1, min(64, -(-(256 << 20) // (args.M * args.K * 2)))) if args.graph else 1
+        xs = [x] + [x.clone() for _ in range(copies - 1)]
+
+        def fn(i=0):
+            return ops.rowquant_headrot(xs[i % copies], hi, lo, "act_sym")
+        if args.graph:
+            t = _graph_time(fn, max(args.reps, copies), dev)
+            print(json.dumps({"kernel_case": "headrot", "M": args.M, "K": args.K, "ms": t,
+                              "rate": units / (t * 1e-3) / 1e9, "unit": "GB/s", "input_copies": copies}))
+            return
+    elif args.kernel_case == "quant":
         units = args.M * args.K * 2.5 + 4 * args.M
         # input copies: enough that consecutive graph launches never find their rows in the 126 MB L2
         copies = max(1, min(64, -(-(256 << 20) // (args.M * args.K * 2)))) if args.graph else 1

@@ -15,7 +15,13 @@ semantics as the reference. Differences, all deliberate:
   `activation_bits` / `weight_bits`) gives the reference's semantics exactly
   (asymmetric per-token codes, core/quantization.py:13-21, no online rotation);
   `QuantConfig()` gives the symmetric per-token scheme with the online
-  Hadamard rotation applied to activations and weights.
+  Hadamard rotation applied to activations and weights;
+* `QuantConfig(online_rotation=False, online_head_rotation=True)` applies the
+  per-head Rotation online instead of absorbing it into W_v: role 'v' keeps
+  its plain weight, and role 'o' keeps W_o R_h (as core/linear.py:34-37) while
+  its input is rotated per head inside the quantize kernel
+  (ops.rowquant_headrot). The layer output is the same product in exact
+  arithmetic (x R (W_o R)^T = x W_o^T per head).
 """
 from __future__ import annotations
 
@@ -34,6 +40,7 @@ class QuantConfig:
     weight_bits: int = 4
     activation_symmetric: bool = True   # scale = absmax/7, codes in [-8, 7]
     online_rotation: bool = True        # y = x (H_a (x) H_b)/sqrt(K) on activations, W' = W (same) offline
+    online_head_rotation: bool = False  # per-head Rotation applied to the o-projection's input online
 
 
 class QuantLinear(nn.Module):
@@ -59,6 +66,8 @@ class QuantLinear(nn.Module):
         if interface is None:
             return weight, bias
         if hasattr(interface, "matrices"):
+            if self.online_heads and self.role == "v":
+                return weight, bias  # the o-projection rotates its input online instead
             mats = interface.matrices()
             if self.role == "v":
                 shaped = weight.float().reshape(interface.heads, interface.head_dim, -1)
@@ -89,6 +98,13 @@ class QuantLinear(nn.Module):
     def rotate(self) -> bool:
         return bool(getattr(self.config, "online_rotation", False))
 
+    @property
+    def online_heads(self) -> bool:
+        """Per-head Rotation interface applied online (roles 'v' / 'o' with online_head_rotation)."""
+        interface = self._interface() if self._interface else None
+        return (bool(getattr(self.config, "online_head_rotation", False)) and interface is not None and
+                hasattr(interface, "matrices") and self.role in ("v", "o"))
+
     def _check_bits(self) -> None:
         if int(self.config.activation_bits) != 4 or int(self.config.weight_bits) != 4:
             raise NotImplementedError("the CUDA path implements W4A4 only (activation_bits = weight_bits = 4)")
@@ -108,6 +124,19 @@ class QuantLinear(nn.Module):
                          row_sums=True)
         self._prep = dict(packed=q.packed, sw=q.scales, wsum=q.row_sums, bias=bias, K=K, N=N, KP=KP,
                           aclip=float(self.activation_clip), bias_cache={})
+        self._attach_head_rotation()
+
+    def _attach_head_rotation(self) -> None:
+        """Role 'o' with online_head_rotation: the (hi, lo) rotation operands of the input quantizer."""
+        if not (self.online_heads and self.role == "o"):
+            return
+        if self.rotate or not self.symmetric:
+            raise NotImplementedError("online head rotation needs symmetric activations and online_rotation=False")
+        K, KP = self._prep["K"], self._prep["KP"]
+        mats = self._interface().matrices().repeat_interleave(self.repeat, dim=0)  # core/linear.py:35
+        if mats.shape[1:] != (128, 128) or K != 128 * mats.shape[0] or K != KP:
+            raise NotImplementedError("online head rotation needs head_dim 128 and K = heads * 128")
+        self._prep["head_rot"] = ops.head_rotation_operands(mats.to(self._prep["packed"].device))
 
     # int8_activations = True: above A8_MIN_TOKENS tokens the symmetric scheme hands the GEMM int8
     # activation codes (w4a4_gemm_a8) instead of packed nibbles. Same output bits; measured on par with
@@ -151,6 +180,7 @@ class QuantLinear(nn.Module):
         with torch.no_grad():
             self.weight_clip.fill_(float(state["weight_clip"]))
             self.activation_clip.fill_(float(state["activation_clip"]))
+        self._attach_head_rotation()
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not self.enabled:
@@ -173,7 +203,13 @@ class QuantLinear(nn.Module):
                 bias = p["bias"].to(x.dtype).contiguous()
                 p["bias_cache"][x.dtype] = bias
         M = x2.shape[0]
-        if self.symmetric and self.int8_activations and M > self.A8_MIN_TOKENS:
+        if "head_rot" in p:  # per-head Rotation applied to the input online (role 'o')
+            if x2.dtype != torch.bfloat16:
+                x2 = x2.to(torch.bfloat16)
+            hi, lo = p["head_rot"]
+            q = ops.rowquant_headrot(x2, hi, lo, "act_sym", clip=p["aclip"])
+            y = ops.w4a4_gemm(q.packed, p["packed"], q.scales, p["sw"], M=M, N=N, bias=bias, out_dtype=x.dtype)
+        elif self.symmetric and self.int8_activations and M > self.A8_MIN_TOKENS:
             # int8 activation codes straight into the GEMM's TMA (no activation expansion); same bits
             q = ops.rowquant(x2, "act_sym", clip=p["aclip"], rotate=self.rotate, KP=p["KP"], codes=True,
                              packed_out=False)

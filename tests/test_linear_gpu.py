@@ -223,3 +223,46 @@ def test_int8_activation_path_same_bits(cuda_device):
     ql.int8_activations = True
     y_a8 = ql(x)
     assert torch.equal(y_packed, y_a8)
+
+
+class _HeadRotation:
+    """Stand-in for core/transforms.py Rotation: the attributes QuantLinear reads (heads, head_dim, matrices())."""
+
+    def __init__(self, R):
+        self.heads, self.head_dim, self._R = R.shape[0], R.shape[1], R
+
+    def matrices(self):
+        return self._R
+
+
+def test_online_head_rotation_matches_absorbed(cuda_device):
+    """Role 'o' with online_head_rotation: input rotated per head inside the quantize kernel, weight W_o R as in
+    core/linear.py:34-37. Matches the absorbed path fed with the already-rotated input (what W_v R^T would produce)
+    to quantisation noise, and the float product within the W4A4 error; role 'v' keeps its plain weight."""
+    from dscquant_b200 import QuantConfig, QuantLinear
+
+    heads, M, N = 8, 96, 512
+    K = 128 * heads
+    g = torch.Generator().manual_seed(11)
+    a = torch.randn(heads, 128, 128, generator=g, dtype=torch.float64) * 0.05
+    R = torch.matrix_exp(a - a.transpose(1, 2)).float().to(cuda_device)
+    rot = _HeadRotation(R)
+    base = _linear(synthetic.weights_bf16(N, K, seed=70), None, cuda_device)
+    on = QuantLinear(base, QuantConfig(online_rotation=False, online_head_rotation=True), interface=rot, role="o")
+    off = QuantLinear(base, QuantConfig(online_rotation=False), interface=rot, role="o")
+    on.enabled = off.enabled = True
+    x = _tbf(synthetic.activations_bf16(M, K, seed=71), cuda_device)
+    x_rot = torch.einsum("thd,hde->the", x.float().reshape(M, heads, 128), R).reshape(M, K).to(torch.bfloat16)
+    y_on, y_off = on(x).float(), off(x_rot).float()
+    y_fp = x.float() @ base.weight.float().T
+    rel = lambda a, b: (torch.linalg.norm(a - b) / torch.linalg.norm(b)).item()  # noqa: E731
+    assert rel(y_on, y_off) < 3e-2
+    assert rel(y_on, y_fp) < 0.15
+    assert "head_rot" in on._prep
+    v = QuantLinear(base, QuantConfig(online_rotation=False, online_head_rotation=True), interface=rot, role="v")
+    assert torch.equal(v.transformed()[0], base.weight)
+    state = on.prepared_state()
+    re = QuantLinear(base, QuantConfig(online_rotation=False, online_head_rotation=True), interface=rot, role="o")
+    re.enabled = True
+    re.load_prepared(state)
+    assert torch.equal(re(x), on(x))
