@@ -237,9 +237,11 @@ class _HeadRotation:
 
 def test_online_head_rotation_matches_absorbed(cuda_device):
     """Role 'o' with online_head_rotation: input rotated per head inside the quantize kernel, weight W_o R as in
-    core/linear.py:34-37. Matches the absorbed path fed with the already-rotated input (what W_v R^T would produce)
-    to quantisation noise, and the float product within the W4A4 error; role 'v' keeps its plain weight."""
-    from dscquant_b200 import QuantConfig, QuantLinear
+    core/linear.py:34-37. The module output equals the kernel's codes fed to the GEMM (bit-exact wiring); against
+    the float product it is as accurate as the absorbed path fed with the already-rotated input (what W_v R^T
+    would produce; that path quantises bf16(x R), the online one the f32 product, so the two differ by int4
+    rounding-boundary flips, not by a common reference). Role 'v' keeps its plain weight."""
+    from dscquant_b200 import QuantConfig, QuantLinear, ops
 
     heads, M, N = 8, 96, 512
     K = 128 * heads
@@ -253,12 +255,16 @@ def test_online_head_rotation_matches_absorbed(cuda_device):
     on.enabled = off.enabled = True
     x = _tbf(synthetic.activations_bf16(M, K, seed=71), cuda_device)
     x_rot = torch.einsum("thd,hde->the", x.float().reshape(M, heads, 128), R).reshape(M, K).to(torch.bfloat16)
-    y_on, y_off = on(x).float(), off(x_rot).float()
+    y_on, y_off = on(x), off(x_rot)
+    q = ops.rowquant_headrot(x, *on._prep["head_rot"], "act_sym")
+    assert torch.equal(y_on, ops.w4a4_gemm(q.packed, on._prep["packed"], q.scales, on._prep["sw"]))
     y_fp = x.float() @ base.weight.float().T
-    rel = lambda a, b: (torch.linalg.norm(a - b) / torch.linalg.norm(b)).item()  # noqa: E731
-    assert rel(y_on, y_off) < 3e-2
-    assert rel(y_on, y_fp) < 0.15
-    assert "head_rot" in on._prep
+    rel = lambda a, b: (torch.linalg.norm(a.float() - b) / torch.linalg.norm(b)).item()  # noqa: E731
+    e_on, e_off = rel(y_on, y_fp), rel(y_off, y_fp)
+    print(f"online head rotation: rel_fro vs float {e_on:.3e} (absorbed path {e_off:.3e})")
+    # the synthetic activations carry x20 outlier channels that a within-head rotation barely spreads, so plain
+    # W4A4 error is large here; the check is that the online path is as accurate as the absorbed one
+    assert e_on < 1.0 and e_on <= 1.05 * e_off + 1e-3
     v = QuantLinear(base, QuantConfig(online_rotation=False, online_head_rotation=True), interface=rot, role="v")
     assert torch.equal(v.transformed()[0], base.weight)
     state = on.prepared_state()
