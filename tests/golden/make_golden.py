@@ -1,4 +1,4 @@
-"""Generates tests/golden/golden_v1.npz from the REFERENCE's own Python code.
+"""Generates tests/golden/golden_v1.npz and golden_transforms_v1.npz from the REFERENCE's own Python code.
 
 Run in a container where the reference checkout is available (its path is the
 first argument, default ../../reference relative to the repository root's
@@ -96,5 +96,69 @@ def main(ref: str) -> None:
     print("wrote", path, os.path.getsize(path), "bytes")
 
 
+def transforms(ref: str) -> None:
+    """golden_transforms_v1.npz: the reference's Rotation / Scaling transforms (core/transforms.py) and
+    QuantLinear.transformed() (core/linear.py:22-46) on seeded parameters: per-head rotation matrices, the
+    absorbed v / o weights (with a GQA repeat) and the scaled up / down weights."""
+    import torch
+    from torch import nn
+
+    sys.path.insert(0, ref)
+    from core.linear import QuantLinear  # reference
+    from core.transforms import Rotation, Scaling  # reference
+
+    g = torch.Generator().manual_seed(1234)
+    out = {"torch_version": np.array(torch.__version__)}
+
+    def bits(t):
+        return t.detach().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    def lin(n, k, bias, seed):
+        base = nn.Linear(k, n, bias=bias, dtype=torch.bfloat16)
+        with torch.no_grad():
+            base.weight.copy_(torch.from_numpy(synthetic.weights_bf16(n, k, seed=seed).view(np.int16)).view(torch.bfloat16))
+            if bias:
+                base.bias.copy_(torch.randn(n, generator=g).to(torch.bfloat16))
+        return base
+
+    cfg = types.SimpleNamespace(activation_bits=4, weight_bits=4)
+    heads, hd, repeat = 2, 128, 2
+    rot = Rotation(heads, hd)
+    rot.set_basis("rec", torch.linalg.qr(torch.randn(rot.dimension, 3, generator=g))[0])
+    rot.set_basis("sid", torch.randn(rot.dimension, 2, generator=g) * 0.02)
+    with torch.no_grad():
+        rot.alpha.copy_(torch.randn(3, generator=g))
+        rot.beta.copy_(torch.randn(2, generator=g))
+        R = rot.matrices()
+    out["rot_matrices"] = R.numpy()
+    v = lin(heads * hd, 64, True, 400)
+    o = lin(48, heads * repeat * hd, False, 401)
+    qv = QuantLinear(v, cfg, interface=rot, role="v")
+    qo = QuantLinear(o, cfg, interface=rot, role="o", repeat=repeat)
+    with torch.no_grad():
+        wv, bv = qv.transformed()
+        wo, _ = qo.transformed()
+    out.update(v_w=bits(v.weight), v_b=bits(v.bias), v_w_t=bits(wv), v_b_t=bits(bv), o_w=bits(o.weight),
+               o_w_t=bits(wo), o_repeat=np.array(repeat))
+    sc = Scaling(96)
+    sc.set_basis("rec", torch.randn(96, 2, generator=g) * 0.3)
+    with torch.no_grad():
+        sc.alpha.copy_(torch.randn(2, generator=g))
+        s_diag = sc.diagonal()
+    out["scale_diag"] = s_diag.numpy()
+    up = lin(96, 40, True, 402)
+    down = lin(30, 96, False, 403)
+    with torch.no_grad():
+        wu, bu = QuantLinear(up, cfg, interface=sc, role="up").transformed()
+        wd, _ = QuantLinear(down, cfg, interface=sc, role="down").transformed()
+    out.update(up_w=bits(up.weight), up_b=bits(up.bias), up_w_t=bits(wu), up_b_t=bits(bu), down_w=bits(down.weight),
+               down_w_t=bits(wd))
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_transforms_v1.npz")
+    np.savez_compressed(path, **out)
+    print("wrote", path, os.path.getsize(path), "bytes")
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(os.path.dirname(ROOT), "reference"))
+    ref_dir = sys.argv[1] if len(sys.argv) > 1 else os.path.join(os.path.dirname(ROOT), "reference")
+    main(ref_dir)
+    transforms(ref_dir)
