@@ -112,10 +112,9 @@ def kernel_case(args) -> None:
     bf = lambda b: torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16).to(dev)  # noqa: E731
     x = bf(synthetic.activations_bf16(args.M, args.K, seed=1))
     if args.kernel_case == "headrot":  # online per-head rotation + quantisation, heads = K / 128
-        import torch as _t
-        g = _t.Generator().manual_seed(5)
-        a = _t.randn(args.K // 128, 128, 128, generator=g, dtype=_t.float64) * 0.05
-        hi, lo = ops.head_rotation_operands(_t.matrix_exp(a - a.transpose(1, 2)).float().to(dev))
+        g = torch.Generator().manual_seed(5)
+        a = torch.randn(args.K // 128, 128, 128, generator=g, dtype=torch.float64) * 0.05
+        hi, lo = ops.head_rotation_operands(torch.matrix_exp(a - a.transpose(1, 2)).float().to(dev))
         units = args.M * args.K * 2.5 + 4 * args.M
         copies = max(1, min(64, -(-(256 << 20) // (args.M * args.K * 2)))) if args.graph else 1
         xs = [x] + [x.clone() for _ in range(copies - 1)]
