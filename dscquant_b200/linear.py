@@ -21,7 +21,13 @@ semantics as the reference. Differences, all deliberate:
   its plain weight, and role 'o' keeps W_o R_h (as core/linear.py:34-37) while
   its input is rotated per head inside the quantize kernel
   (ops.rowquant_headrot). The layer output is the same product in exact
-  arithmetic (x R (W_o R)^T = x W_o^T per head).
+  arithmetic (x R (W_o R)^T = x W_o^T per head);
+* `QuantConfig(online_scaling=True)` applies the `Scaling` diagonal of role
+  'up' (core/linear.py:40-43: rows of W and the bias divided by s) in the
+  GEMM epilogue: the codes come from the plain weight (per-row symmetric codes
+  do not change under a per-row scale) and the channel scales become sw / s,
+  so the output is the reference's up to the bf16 rounding of W / s that the
+  reference applies before quantising. Role 'down' stays absorbed (W diag(s)).
 """
 from __future__ import annotations
 
@@ -41,6 +47,7 @@ class QuantConfig:
     activation_symmetric: bool = True   # scale = absmax/7, codes in [-8, 7]
     online_rotation: bool = True        # y = x (H_a (x) H_b)/sqrt(K) on activations, W' = W (same) offline
     online_head_rotation: bool = False  # per-head Rotation applied to the o-projection's input online
+    online_scaling: bool = False        # Scaling of role 'up' applied in the GEMM epilogue (channel scales / s)
 
 
 class QuantLinear(nn.Module):
@@ -82,7 +89,8 @@ class QuantLinear(nn.Module):
         else:
             scale = interface.diagonal()
             if self.role == "up":
-                weight = (weight.float() / scale[:, None]).to(weight.dtype)
+                if not self.online_up_scaling:  # online: the epilogue divides by s (prepare())
+                    weight = (weight.float() / scale[:, None]).to(weight.dtype)
                 if bias is not None:
                     bias = (bias.float() / scale).to(bias.dtype)
             else:
@@ -97,6 +105,13 @@ class QuantLinear(nn.Module):
     @property
     def rotate(self) -> bool:
         return bool(getattr(self.config, "online_rotation", False))
+
+    @property
+    def online_up_scaling(self) -> bool:
+        """Scaling of role 'up' applied in the GEMM epilogue (online_scaling)."""
+        interface = self._interface() if self._interface else None
+        return (bool(getattr(self.config, "online_scaling", False)) and interface is not None and
+                hasattr(interface, "diagonal") and not hasattr(interface, "matrices") and self.role == "up")
 
     @property
     def online_heads(self) -> bool:
@@ -122,7 +137,10 @@ class QuantLinear(nn.Module):
         w = weight if weight.dtype in (torch.bfloat16, torch.float16, torch.float32) else weight.float()
         q = ops.rowquant(w.contiguous(), "weight_sym", clip=float(self.weight_clip), rotate=self.rotate, KP=KP,
                          row_sums=True)
-        self._prep = dict(packed=q.packed, sw=q.scales, wsum=q.row_sums, bias=bias, K=K, N=N, KP=KP,
+        sw = q.scales
+        if self.online_up_scaling:  # the diagonal of role 'up' folded into the per-channel epilogue scale
+            sw = (sw / self._interface().diagonal().to(device=sw.device, dtype=torch.float32)).contiguous()
+        self._prep = dict(packed=q.packed, sw=sw, wsum=q.row_sums, bias=bias, K=K, N=N, KP=KP,
                           aclip=float(self.activation_clip), bias_cache={})
         self._attach_head_rotation()
 

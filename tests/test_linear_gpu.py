@@ -272,3 +272,45 @@ def test_online_head_rotation_matches_absorbed(cuda_device):
     re.enabled = True
     re.load_prepared(state)
     assert torch.equal(re(x), on(x))
+
+
+class _Scaling:
+    """Stand-in for core/transforms.py Scaling: diagonal() only."""
+
+    def __init__(self, s):
+        self._s = s
+
+    def diagonal(self):
+        return self._s
+
+
+def test_online_scaling_in_epilogue(cuda_device):
+    """Role 'up' with online_scaling: codes of the plain weight, channel scales sw / s applied by the GEMM epilogue
+    (bit-exact wiring), output as accurate as the reference's absorbed W / s path."""
+    from dscquant_b200 import QuantConfig, QuantLinear, ops
+
+    M, K, N = 64, 1024, 384
+    g = torch.Generator().manual_seed(3)
+    s = torch.exp(torch.randn(N, generator=g) * 0.3).to(cuda_device)
+    base = _linear(synthetic.weights_bf16(N, K, seed=80), synthetic.weights_bf16(1, N, seed=81, std=0.5)[0],
+                   cuda_device)
+    scaling = _Scaling(s)  # QuantLinear holds its interface by weakref (core/linear.py:15): keep it alive
+    on = QuantLinear(base, QuantConfig(online_rotation=False, online_scaling=True), interface=scaling, role="up")
+    off = QuantLinear(base, QuantConfig(online_rotation=False), interface=scaling, role="up")
+    assert on.online_up_scaling and not off.online_up_scaling
+    plain = QuantLinear(base, QuantConfig(online_rotation=False))
+    for m in (on, off, plain):
+        m.enabled = True
+        m.prepare()
+    assert torch.equal(on._prep["packed"], plain._prep["packed"])
+    assert torch.equal(on._prep["sw"], plain._prep["sw"] / s)
+    x = _tbf(synthetic.activations_bf16(M, K, seed=82), cuda_device)
+    y_on, y_off = on(x), off(x)
+    q = ops.rowquant(x, "act_sym", KP=K)
+    bias = (base.bias.float() / s).to(torch.bfloat16)
+    assert torch.equal(y_on, ops.w4a4_gemm(q.packed, on._prep["packed"], q.scales, on._prep["sw"], bias=bias))
+    y_ref = (x.float() @ base.weight.float().T) / s + bias.float()
+    rel = lambda a, b: (torch.linalg.norm(a.float() - b) / torch.linalg.norm(b)).item()  # noqa: E731
+    e_on, e_off = rel(y_on, y_ref), rel(y_off, y_ref)
+    print(f"online scaling: rel_fro vs float {e_on:.3e} (absorbed path {e_off:.3e})")
+    assert e_on <= 1.05 * e_off + 1e-3

@@ -114,3 +114,20 @@ def test_rotate_heads_is_per_head_matmul(oracle):
     ref = np.concatenate([x[:, 128 * h:128 * (h + 1)].astype(np.float64) @ R[h] for h in range(3)], axis=1)
     np.testing.assert_allclose(y, ref, rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(np.linalg.norm(y, axis=1), np.linalg.norm(x, axis=1), rtol=1e-5)
+
+
+def test_online_scaling_keeps_plain_up_weight(gt):
+    """online_scaling: role 'up' keeps its plain weight (the epilogue divides by s) and the reference's bias / s;
+    role 'down' stays absorbed exactly as the reference."""
+    from dscquant_b200 import QuantConfig, QuantLinear
+
+    sc = _Scale(gt["scale_diag"])
+    cfg = QuantConfig(online_rotation=False, online_scaling=True)
+    up = QuantLinear(_lin(gt["up_w"], gt["up_b"]), cfg, interface=sc, role="up")
+    assert up.online_up_scaling
+    w, b = up.transformed()
+    np.testing.assert_array_equal(_bits(w), gt["up_w"])
+    np.testing.assert_array_equal(_bits(b), gt["up_b_t"])
+    down = QuantLinear(_lin(gt["down_w"]), cfg, interface=sc, role="down")
+    assert not down.online_up_scaling
+    np.testing.assert_array_equal(_bits(down.transformed()[0]), gt["down_w_t"])
