@@ -42,6 +42,13 @@ int cuda_fail(cudaError_t e, const char* where) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Row-length limits: the reference's quantize accepts K <= 2^20 (kernel/w4a4.cu:166), which the
+// unrotated quantizers match; the online rotation keeps the row in shared memory (K <= 32768). The
+// GEMMs accumulate 256 * sum(a b) in int32 (codes shifted into the high nibble), so KP <= 65536.
+constexpr int64_t kMaxRowK = 1048576;
+constexpr int64_t kMaxRotK = 32768;
+constexpr int64_t kMaxGemmKP = 65536;
+
 // sm_100 check, cached per device.
 int check_device(int* dev_out) {
   int dev = 0;
@@ -502,10 +509,11 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   DSCQ_REQUIRE(x && (packed || codes) && scales, "x, scales and packed or codes must not be null");
   DSCQ_REQUIRE(x_dtype == DSCQ_BF16 || x_dtype == DSCQ_F16 || x_dtype == DSCQ_F32, "x_dtype must be bf16/f16/f32");
   DSCQ_REQUIRE(M >= 1 && M <= (1 << 24), "require 1 <= M <= 2^24");
-  DSCQ_REQUIRE(K >= 1 && K <= 32768, "require 1 <= K <= 32768");
+  DSCQ_REQUIRE(K >= 1 && K <= kMaxRowK, "require 1 <= K <= 1048576");
+  DSCQ_REQUIRE(!rotate || K <= kMaxRotK, "the online rotation supports K <= 32768");
   DSCQ_REQUIRE(ld_x >= K, "ld_x must be >= K");
   DSCQ_REQUIRE(rows_out >= M && rows_out <= (1 << 24), "rows_out must be >= M");
-  DSCQ_REQUIRE(KP >= K && KP % 2 == 0 && KP <= 65536, "KP must be even and >= K");
+  DSCQ_REQUIRE(KP >= K && KP % 2 == 0 && KP <= kMaxRowK + 64, "KP must be even and >= K");
   DSCQ_REQUIRE(!packed || ld_packed >= KP / 2, "ld_packed must be >= KP/2");
   DSCQ_REQUIRE(mode >= DSCQ_ACT_SYM && mode <= DSCQ_ACT_ASYM_TORCH, "unknown quantizer mode");
   DSCQ_REQUIRE(std::isfinite(clip) && clip > 0.f, "clip must be a positive finite number");
@@ -629,6 +637,12 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   }
 
   constexpr int T = 512;
+  if (!rotate && K > kMaxRotK) {  // long rows: two passes over global memory, as kernel/w4a4.cu:20-63
+    dscq::rowquant_stream<T><<<static_cast<unsigned>(rows_out), T, 0, cst>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch rowquant_stream");
+    return DSCQ_OK;
+  }
   size_t smem = static_cast<size_t>(K) * sizeof(float) * ((rotate && p.rot_a > 32) ? 2 : 1);
   if (smem > 220 * 1024)
     return fail(DSCQ_ERR_UNSUPPORTED, "row of K=" + std::to_string(K) + " does not fit in shared memory");
@@ -668,11 +682,11 @@ static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, cons
   DSCQ_REQUIRE(out_dtype == DSCQ_BF16 || out_dtype == DSCQ_F16 || out_dtype == DSCQ_F32, "out_dtype must be bf16/f16/f32");
   DSCQ_REQUIRE(aligned(a, 16) && aligned(b, 16), "packed operands must be 16-byte aligned");
   DSCQ_REQUIRE(variant >= DSCQ_GEMM_AUTO && variant <= DSCQ_GEMM_LARGE_M_PAIR_TMEM, "unknown GEMM variant");
+  if (KP > kMaxGemmKP)
+    return fail(DSCQ_ERR_UNSUPPORTED, "KP > 65536 is not supported: the int8 tensor-core accumulation (256 * sum) "
+                                      "would overflow int32 (the reference's s4 WMMA path accepts KP <= 2^20)");
   int st = check_device(nullptr);
   if (st) return st;
-
-  if (KP > 65536)
-    return fail(DSCQ_ERR_UNSUPPORTED, "KP > 65536: the int8 tensor-core accumulation (256 * sum) would overflow int32");
   const int64_t kbytes = KP / 2;
   const int kblocks = static_cast<int>((KP + 127) / 128);
   const bool decode = M <= 32 && (variant == DSCQ_GEMM_AUTO || variant == DSCQ_GEMM_SMALL_M);
@@ -805,6 +819,7 @@ int dscq_matmul_a8_variant(const int8_t* a, int64_t ld_a, const uint8_t* b, cons
   DSCQ_REQUIRE(M > 0 && M <= (1 << 24) && N > 0 && N <= (1 << 24) && KP > 0 && KP <= 1048576 && KP % 64 == 0,
                "Invalid dimensions (need M, N > 0 and KP a positive multiple of 64)");
   DSCQ_REQUIRE(ld_a >= KP && ld_a % 16 == 0, "ld_a must be >= KP and a multiple of 16");
+  if (KP > kMaxGemmKP) return fail(DSCQ_ERR_UNSUPPORTED, "KP > 65536 is not supported by the int8 GEMMs");
   DSCQ_REQUIRE(aligned(a, 16) && aligned(b, 16), "operands must be 16-byte aligned");
   DSCQ_REQUIRE(out_dtype == DSCQ_BF16 || out_dtype == DSCQ_F16 || out_dtype == DSCQ_F32, "out_dtype must be bf16/f16/f32");
   int st = check_device(nullptr);

@@ -220,6 +220,66 @@ __global__ void __launch_bounds__(T) rowquant_smem(const RowQuantParams p) {
   }
 }
 
+// Rows too long for shared memory (no rotation): one CTA per output row reads the row twice from
+// global memory, once for the statistics and once for the codes, as the reference's quantize_rows
+// does (kernel/w4a4.cu:20-63, K up to 2^20). Same modes, padding and outputs as rowquant_smem.
+template <int T>
+__global__ void __launch_bounds__(T) rowquant_stream(const RowQuantParams p) {
+  __shared__ float fscratch[32];
+  __shared__ int iscratch[32];
+  const int row = blockIdx.x;
+  const int K = p.K;
+  const bool live = row < p.M;
+  const int64_t xrow = static_cast<int64_t>(row) * p.ld_x;
+  const bool asym = p.mode == kActAsym || p.mode == kActAsymTorch;
+  float a_max = 0.f, a_min = 0.f;
+  if (live) {
+    for (int k = threadIdx.x; k < K; k += T) {
+      const float y = load_in(p.x, xrow + k, p.x_dtype);
+      if (asym) {
+        a_max = fmaxf(a_max, y);
+        a_min = fminf(a_min, y);
+      } else {
+        a_max = fmaxf(a_max, fabsf(y));
+      }
+    }
+  }
+  a_max = block_reduce_max<T>(a_max, fscratch);
+  if (asym) a_min = -block_reduce_max<T>(-a_min, fscratch);
+  float scale;
+  int zero = 0;
+  if (asym) {
+    const float lo = __fmul_rn(a_min, p.clip), hi = __fmul_rn(a_max, p.clip);
+    scale = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), 15.f), 1e-8f);
+    zero = max(0, min(15, __float2int_rn(__fdiv_rn(-lo, scale))));
+  } else {
+    scale = fmaxf(__fdiv_rn(__fmul_rn(a_max, p.clip), 7.f), 1e-8f);
+  }
+  int csum = 0;
+  const int pad_code = asym ? zero : 0;
+  uint8_t* prow = p.packed ? p.packed + static_cast<int64_t>(row) * p.ld_packed : nullptr;
+  int8_t* crow = p.codes ? p.codes + static_cast<int64_t>(row) * p.ld_codes : nullptr;
+  for (int pr = threadIdx.x; pr < p.KP / 2; pr += T) {
+    const int k = 2 * pr;
+    const int c0 = (live && k < K) ? quant_code(load_in(p.x, xrow + k, p.x_dtype), scale, zero, p.mode) : pad_code;
+    const int c1 = (live && k + 1 < K) ? quant_code(load_in(p.x, xrow + k + 1, p.x_dtype), scale, zero, p.mode)
+                                       : pad_code;
+    if (k < K) csum += c0;
+    if (k + 1 < K) csum += c1;
+    if (prow) prow[pr] = static_cast<uint8_t>(nibble_of(c0, p.mode) | (nibble_of(c1, p.mode) << 4));
+    if (crow) {
+      crow[k] = static_cast<int8_t>(c0);
+      crow[k + 1] = static_cast<int8_t>(c1);
+    }
+  }
+  if (p.row_sums) csum = block_reduce_sum<T>(csum, iscratch);
+  if (threadIdx.x == 0) {
+    p.scales[row] = scale;
+    if (p.zeros) p.zeros[row] = zero;
+    if (p.row_sums) p.row_sums[row] = csum;
+  }
+}
+
 // ------------------------------------------------------------ pack / unpack
 // pack_int4, core/quantization.py:31-40: int8 codes in [-8, 7] -> bytes,
 // byte j = (c[2j] & 15) | (c[2j+1] & 15) << 4, odd K padded with code 0.

@@ -222,21 +222,60 @@ def rowquant_headrot(x: torch.Tensor, hi: torch.Tensor, lo: torch.Tensor, mode: 
     return RowQuant(packed, scales, None, None, cds, K)
 
 
+def _check_gemm_metadata(dev: torch.device, M: int, N: int, out_dtype: torch.dtype, sx, sw, zx=None, sums=None,
+                         bias=None, residual=None) -> None:
+    """Argument checks shared by the GEMM entry points (the same checks as the reference's matmul,
+    kernel/w4a4.cu:192-202): the kernels read sx[0..M), sw / sums / bias [0..N), zx [0..M) and
+    residual [M, N] through raw pointers, so a short, mistyped or misplaced tensor is rejected here."""
+    if out_dtype not in _DT:
+        raise RuntimeError("out_dtype must be bf16, f16 or f32")
+    for name, t, dtype, n in (("sx", sx, torch.float32, M), ("sw", sw, torch.float32, N), ("zx", zx, torch.int32, M),
+                              ("sums", sums, torch.int32, N)):
+        if t is None:
+            continue
+        if not t.is_cuda or t.device != dev:
+            raise RuntimeError(f"{name} must be a CUDA tensor on {dev}")
+        if t.dtype != dtype:
+            raise RuntimeError(f"{name} must be {dtype}")
+        if not t.is_contiguous() or t.numel() < n:
+            raise RuntimeError(f"{name} must be contiguous with at least {n} elements")
+    if (zx is None) != (sums is None):
+        raise RuntimeError("zx and sums go together (asymmetric activations)")
+    if bias is not None:
+        if not bias.is_cuda or bias.device != dev or bias.dtype != out_dtype:
+            raise RuntimeError(f"bias must be a {out_dtype} CUDA tensor on {dev} (the output dtype)")
+        if not bias.is_contiguous() or bias.numel() != N:
+            raise RuntimeError(f"bias must be contiguous with N={N} elements")
+    if residual is not None:
+        if not residual.is_cuda or residual.device != dev or residual.dtype != out_dtype:
+            raise RuntimeError(f"residual must be a {out_dtype} CUDA tensor on {dev} (the output dtype)")
+        if tuple(residual.shape) != (M, N) or not residual.is_contiguous():
+            raise RuntimeError(f"residual must be a contiguous [{M}, {N}] tensor")
+
+
 def w4a4_gemm(a: torch.Tensor, b: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor, *, M: int | None = None,
               N: int | None = None, zx: torch.Tensor | None = None, sums: torch.Tensor | None = None,
               bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
               out_dtype: torch.dtype = torch.bfloat16, return_raw: bool = False, want_out: bool = True,
               variant: str = "auto"):
     """out[m, n] = ((sum_k a[m,k] b[n,k] + (8 - zx[m]) sums[n]) * sx[m]) * sw[n] + bias[n] + residual[m, n]
-    on packed int4 operands (tcgen05 int8 GEMM). Returns out, or (out, raw) with return_raw."""
-    M = a.size(0) if M is None else M
-    N = b.size(0) if N is None else N
-    KP = a.size(1) * 2
-    for name, t in (("a", a), ("b", b), ("sx", sx), ("sw", sw)):
+    on packed int4 operands (tcgen05 int8 GEMM). Returns out, or (out, raw) with return_raw.
+    a [>= M, KP/2] and b [>= N, KP/2] are contiguous u8 rows; M and N default to their row counts."""
+    for name, t in (("a", a), ("b", b)):
         _check_cuda(t, name)
+        if t.dtype != torch.uint8 or t.dim() != 2:
+            raise RuntimeError(f"{name} must be a 2-D uint8 tensor of packed int4 codes")
+    dev = a.device
+    if b.device != dev:
+        raise RuntimeError("a and b must be on the same device")
+    M = a.size(0) if M is None else int(M)
+    N = b.size(0) if N is None else int(N)
+    KP = a.size(1) * 2
     if b.size(1) != a.size(1):
         raise RuntimeError("a and b must have the same packed K")
-    dev = a.device
+    if not (0 < M <= a.size(0) and 0 < N <= b.size(0)):
+        raise RuntimeError(f"need 0 < M <= a.size(0) and 0 < N <= b.size(0) (M={M}, N={N})")
+    _check_gemm_metadata(dev, M, N, out_dtype, sx, sw, zx, sums, bias, residual)
     with torch.cuda.device(dev):
         out = torch.empty((M, N), dtype=out_dtype, device=dev) if want_out else None
         raw = torch.empty((M, N), dtype=torch.int32, device=dev) if return_raw else None
@@ -256,14 +295,20 @@ def w4a4_gemm_a8(a: torch.Tensor, b: torch.Tensor, sx: torch.Tensor, sw: torch.T
     packed_out=False)) and packed int4 weights b [N, KP/2]; symmetric activations only. Same bits as
     w4a4_gemm on the packed form of a. `variant`: "auto" (CTA pairs for 256-wide tiles), "large_m"
     (1-CTA kernel) or "large_m_pair" (CTA pairs)."""
-    M = a.size(0) if M is None else M
-    N = b.size(0) if N is None else N
+    _check_cuda(b, "b")
+    if b.dtype != torch.uint8 or b.dim() != 2:
+        raise RuntimeError("b must be a 2-D uint8 tensor of packed int4 codes")
     KP = b.size(1) * 2
-    for name, t in (("b", b), ("sx", sx), ("sw", sw)):
-        _check_cuda(t, name)
     if not a.is_cuda or a.dtype != torch.int8 or a.dim() != 2 or a.stride(1) != 1 or a.size(1) < KP:
         raise RuntimeError("a must be CUDA int8 codes [M, >= KP] with unit column stride")
     dev = a.device
+    if b.device != dev:
+        raise RuntimeError("a and b must be on the same device")
+    M = a.size(0) if M is None else int(M)
+    N = b.size(0) if N is None else int(N)
+    if not (0 < M <= a.size(0) and 0 < N <= b.size(0)):
+        raise RuntimeError(f"need 0 < M <= a.size(0) and 0 < N <= b.size(0) (M={M}, N={N})")
+    _check_gemm_metadata(dev, M, N, out_dtype, sx, sw, None, None, bias, residual)
     with torch.cuda.device(dev):
         out = torch.empty((M, N), dtype=out_dtype, device=dev)
         raw = torch.empty((M, N), dtype=torch.int32, device=dev) if return_raw else None

@@ -22,6 +22,14 @@ Exchange of the blocks (the only cross-device step):
   (all output blocks landed).
 * ``nccl``: local [M, N/p] block, ``all_gather_into_tensor`` into [p, M, N/p],
   then one copy into the [M, N] layout.
+
+Result lifetime: both modes return a tensor the caller owns. In the fused mode
+the gathered output lives in the symmetric buffer, which the next call of the
+same layer overwrites from every rank's epilogue; the layer therefore returns a
+copy unless it was built with ``copy_out=False``. Then the returned tensor is a
+view of the symmetric buffer that stays valid only until the next call of this
+layer on any rank (a caller that consumes it before that call, as a layer stack
+does, saves the copy).
 """
 from __future__ import annotations
 
@@ -59,7 +67,7 @@ class ColumnParallelQuantLinear:
     """W4A4 y = x W^T with W's output channels split across the ranks of `group`."""
 
     def __init__(self, weight_shard: torch.Tensor, N: int, group=None, rotate: bool = True, mode: str = "fused",
-                 max_tokens: int = 8192, bias_shard: torch.Tensor | None = None):
+                 max_tokens: int = 8192, bias_shard: torch.Tensor | None = None, copy_out: bool = True):
         if mode not in ("fused", "nccl"):
             raise ValueError("mode must be 'fused' or 'nccl'")
         self.group = group
@@ -73,6 +81,7 @@ class ColumnParallelQuantLinear:
         self.KP = (self.K + 63) // 64 * 64
         self.rotate = rotate
         self.mode = mode
+        self.copy_out = copy_out
         self.device = weight_shard.device
         q = ops.rowquant(weight_shard.contiguous(), "weight_sym", rotate=rotate, KP=self.KP)
         self.w_packed, self.sw = q.packed, q.scales
@@ -117,7 +126,7 @@ class ColumnParallelQuantLinear:
                                          ops._stream(self.device))
         _lib.check(rc, "dscq_matmul_cols")
         self.hdl.barrier(channel=2)
-        return self.out[:M]
+        return self.out[:M].clone() if self.copy_out else self.out[:M]
 
     def _quantize_rows_sharded(self, x: torch.Tensor, M: int):
         """Fused mode: rank r rotates and quantises token rows row_bounds(M, p, r) into its symmetric

@@ -56,6 +56,17 @@ def oracle():
     return orc
 
 
+@pytest.fixture(autouse=True)
+def _device_status_clean(request):
+    """After every GPU test: no kernel of the library raised its sticky status (an expired bounded
+    wait or bad launch geometry), which would otherwise leave partial outputs unnoticed."""
+    yield
+    if "gpu" in request.keywords and _cuda_ok():
+        from dscquant_b200 import ops
+
+        assert ops.device_status(0) == 0, "a kernel raised the device status word during this test"
+
+
 @pytest.fixture(scope="session")
 def cuda_device(native):
     import torch

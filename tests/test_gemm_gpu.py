@@ -236,3 +236,47 @@ def test_gemm_a8_strided_codes_and_errors(oracle, cuda_device):
     np.testing.assert_array_equal(raw.cpu().numpy(), ref_raw)
     with pytest.raises(RuntimeError):
         ops.w4a4_gemm_a8(codes.to(torch.int32), b, sx, sw)
+
+
+def test_w4a4_gemm_argument_checks(cuda_device):
+    """ops.w4a4_gemm / w4a4_gemm_a8 reject what the kernels would read out of bounds or misinterpret."""
+    from dscquant_b200 import ops
+
+    dev = cuda_device
+    M, N, KP = 32, 64, 128
+    a = torch.zeros((M, KP // 2), dtype=torch.uint8, device=dev)
+    b = torch.zeros((N, KP // 2), dtype=torch.uint8, device=dev)
+    sx, sw = torch.ones(M, device=dev), torch.ones(N, device=dev)
+    ops.w4a4_gemm(a, b, sx, sw)  # the valid call
+    bad = [
+        dict(M=M + 1),                                           # more rows than a holds
+        dict(N=N + 8),                                           # more rows than b holds
+        dict(sx=torch.ones(M - 1, device=dev)),                  # short token scales
+        dict(sw=torch.ones(N, device=dev, dtype=torch.float16)),  # mistyped channel scales
+        dict(sx=torch.ones(M)),                                   # host tensor
+        dict(zx=torch.zeros(M, dtype=torch.int32, device=dev)),  # zero points without code sums
+        dict(zx=torch.zeros(M, device=dev), sums=torch.zeros(N, dtype=torch.int32, device=dev)),  # float zx
+        dict(bias=torch.zeros(N, device=dev)),                    # fp32 bias with a bf16 output
+        dict(bias=torch.zeros(N - 1, dtype=torch.bfloat16, device=dev)),
+        dict(residual=torch.zeros(M, N - 8, dtype=torch.bfloat16, device=dev)),
+        dict(residual=torch.zeros(M, N, dtype=torch.float16, device=dev)),
+    ]
+    for kw in bad:
+        args = dict(sx=sx, sw=sw)
+        args.update(kw)
+        s_x, s_w = args.pop("sx"), args.pop("sw")
+        with pytest.raises(RuntimeError):
+            ops.w4a4_gemm(a, b, s_x, s_w, **args)
+    with pytest.raises(RuntimeError):
+        ops.w4a4_gemm(a.t(), b, sx, sw)  # not contiguous rows
+    with pytest.raises(RuntimeError):
+        ops.w4a4_gemm(a.view(torch.int8), b, sx, sw)
+    codes = torch.zeros((M, KP), dtype=torch.int8, device=dev)
+    ops.w4a4_gemm_a8(codes, b, sx, sw)
+    for kw in (dict(M=M + 1), dict(sx=torch.ones(M - 1, device=dev)), dict(bias=torch.zeros(N, device=dev)),
+               dict(residual=torch.zeros(M, N, dtype=torch.float32, device=dev))):
+        args = dict(sx=sx, sw=sw)
+        args.update(kw)
+        s_x, s_w = args.pop("sx"), args.pop("sw")
+        with pytest.raises(RuntimeError):
+            ops.w4a4_gemm_a8(codes, b, s_x, s_w, **args)

@@ -1,6 +1,7 @@
 """Column-parallel W4A4 linear on 2 GPUs (NCCL + symmetric memory): the gathered [M, N] output of both
 exchange modes (all-gather fused into the GEMM epilogue over NVLink, and NCCL all-gather) is
-bit-identical to a single-GPU QuantLinear on the full weight. Skipped when fewer than 2 GPUs exist."""
+bit-identical to a single-GPU QuantLinear on the full weight, also when two consecutive results are
+held at once. Skipped when fewer than 2 GPUs exist."""
 import os
 import socket
 
@@ -46,14 +47,18 @@ def _worker(rank, world, port, q):
         ql = QuantLinear(base, QuantConfig())
         ql.enabled = True
         ref = ql(x)
+        x2 = bf(synthetic.activations_bf16(M, K, seed=23))
+        ref2 = ql(x2)
         lo, hi = parallel.shard_bounds(N, world, rank)
         ok = []
         for mode in ("fused", "nccl"):
             layer = parallel.ColumnParallelQuantLinear(w[lo:hi], N, mode=mode, max_tokens=512)
-            for _ in range(2):  # second call reuses the symmetric buffer
-                y = layer(x)
+            # two results held at once: the second call reuses the symmetric buffer, and the first
+            # result (a copy by default) must keep its values
+            y1 = layer(x)
+            y2 = layer(x2)
             torch.cuda.synchronize()
-            ok.append(bool(torch.equal(y, ref)))
+            ok.append(bool(torch.equal(y1, ref)) and bool(torch.equal(y2, ref2)))
         dist.barrier()
         q.put((rank, ok))
     finally:
