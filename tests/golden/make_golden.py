@@ -1,4 +1,5 @@
-"""Generates tests/golden/golden_v1.npz and golden_transforms_v1.npz from the REFERENCE's own Python code.
+"""Generates tests/golden/golden_v1.npz, golden_transforms_v1.npz and golden_extra_v1.npz from the REFERENCE's
+own Python code.
 
 Run in a container where the reference checkout is available (its path is the
 first argument, default ../../reference relative to the repository root's
@@ -7,7 +8,7 @@ records their outputs on seeded inputs produced by dscquant_b200.synthetic, so
 the fixtures pin both the CPU oracle (oracle/oracle.py) and the CUDA kernels to
 the reference without needing the reference at test time.
 
-    python tests/golden/make_golden.py /path/to/reference
+    python tests/golden/make_golden.py /path/to/reference [main] [transforms] [extras]
 """
 from __future__ import annotations
 
@@ -158,7 +159,59 @@ def transforms(ref: str) -> None:
     print("wrote", path, os.path.getsize(path), "bytes")
 
 
+def extras(ref: str) -> None:
+    """golden_extra_v1.npz: ste_round (core/quantization.py:4-5) forward values and gradients on crafted
+    ties, signed zeros and large values; and Rotation.matrices() / Scaling.diagonal()
+    (core/transforms.py:42-52, 71-72) together with the buffers and parameters that define them
+    (rec_basis, sid_basis, alpha, beta), so a restatement can be pinned from the state alone."""
+    import torch
+
+    sys.path.insert(0, ref)
+    from core.quantization import ste_round  # reference
+    from core.transforms import Rotation, Scaling  # reference
+
+    out = {"torch_version": np.array(torch.__version__)}
+    g = torch.Generator().manual_seed(4321)
+    crafted = torch.tensor([0.5, 1.5, 2.5, -0.5, -1.5, -2.5, -0.4, -0.0, 0.0, 0.49999997, 7.5, -7.5, 3.0e6 + 0.5,
+                            -8.5, 1e-30, -1e-30, 12582912.5, 16777215.0, 2.0 ** 23 + 1.0], dtype=torch.float32)
+    x = torch.cat([crafted, torch.randn(1000, generator=g) * 10, torch.rand(64, generator=g).floor() + 0.5])
+    xr = x.clone().requires_grad_(True)
+    y = ste_round(xr)
+    w = torch.randn(x.shape, generator=g)
+    (y * w).sum().backward()
+    out.update(ste_x=x.numpy(), ste_y=y.detach().numpy(), ste_w=w.numpy(), ste_grad=xr.grad.numpy())
+
+    heads, hd = 3, 16
+    rot = Rotation(heads, hd)
+    rot.set_basis("rec", torch.linalg.qr(torch.randn(rot.dimension, 4, generator=g))[0])
+    rot.set_basis("sid", torch.randn(rot.dimension, 3, generator=g) * 0.05)
+    with torch.no_grad():
+        rot.alpha.copy_(torch.randn(4, generator=g) * 2)
+        rot.beta.copy_(torch.randn(3, generator=g))
+        R = rot.matrices()
+    out.update(rot_heads=np.array(heads), rot_head_dim=np.array(hd), rot_rec_basis=rot.rec_basis.numpy(),
+               rot_sid_basis=rot.sid_basis.numpy(), rot_alpha=rot.alpha.detach().numpy(),
+               rot_beta=rot.beta.detach().numpy(), rot_R=R.numpy())
+    sc = Scaling(80)
+    sc.set_basis("rec", torch.randn(80, 3, generator=g) * 0.3)
+    sc.set_basis("sid", torch.randn(80, 2, generator=g) * 0.1)
+    with torch.no_grad():
+        sc.alpha.copy_(torch.randn(3, generator=g))
+        sc.beta.copy_(torch.randn(2, generator=g))
+        s_diag = sc.diagonal()
+    out.update(sc_rec_basis=sc.rec_basis.numpy(), sc_sid_basis=sc.sid_basis.numpy(), sc_alpha=sc.alpha.detach().numpy(),
+               sc_beta=sc.beta.detach().numpy(), sc_diag=s_diag.numpy())
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_extra_v1.npz")
+    np.savez_compressed(path, **out)
+    print("wrote", path, os.path.getsize(path), "bytes")
+
+
 if __name__ == "__main__":
     ref_dir = sys.argv[1] if len(sys.argv) > 1 else os.path.join(os.path.dirname(ROOT), "reference")
-    main(ref_dir)
-    transforms(ref_dir)
+    which = sys.argv[2:] or ["main", "transforms", "extras"]
+    if "main" in which:
+        main(ref_dir)
+    if "transforms" in which:
+        transforms(ref_dir)
+    if "extras" in which:
+        extras(ref_dir)

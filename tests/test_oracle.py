@@ -1,6 +1,11 @@
 """CPU oracle pinned against the reference's golden vectors (tests/golden/make_golden.py)."""
+import os
+import sys
+
 import numpy as np
 import pytest
+
+from conftest import ROOT
 
 
 def _f32(bits):
@@ -147,3 +152,24 @@ def test_fake_quant_linear_restatement_matches_reference(golden, oracle):
         ref = _f32(golden[f"{name}_y"]).astype(np.float64)
         rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
         assert rel < 4e-3, (name, rel)
+
+
+@pytest.mark.parametrize("name", ["lin_a", "lin_b", "lin_cfg0"])
+def test_torch_port_of_reference_forward_matches_golden(golden, name):
+    """oracle_torch.quantlinear_forward (the timed CPU baseline) reproduces the reference's own
+    QuantLinear.forward outputs bit for bit (core/linear.py:48-52)."""
+    import torch
+
+    from dscquant_b200 import synthetic
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle_torch
+
+    M, K, N, has_bias = (int(v) for v in golden[f"{name}_shape"])
+    x, w = golden.get(f"{name}_x"), golden.get(f"{name}_w")
+    if x is None:
+        x, w = synthetic.activations_bf16(M, K, seed=100 + M), synthetic.weights_bf16(N, K, seed=200 + N)
+    bf = lambda b: torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16)  # noqa: E731
+    bias = bf(golden[f"{name}_bias"]) if has_bias else None
+    y = oracle_torch.quantlinear_forward(bf(x), bf(w), bias)
+    np.testing.assert_array_equal(y.view(torch.int16).numpy().view(np.uint16), golden[f"{name}_y"])

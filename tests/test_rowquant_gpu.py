@@ -189,3 +189,20 @@ def test_rowquant_codes_only(cuda_device, K):
     assert torch.equal(a.codes, b.codes) and torch.equal(a.scales, b.scales)
     with pytest.raises(ValueError):
         ops.rowquant(x, "act_sym", rotate=True, KP=K, packed_out=False)
+
+
+def test_ste_round_matches_reference(cuda_device):
+    """quantization.ste_round (core/quantization.py:4-5) on CUDA: forward bits equal the reference's on crafted
+    ties, signed zeros and large values (golden_extra_v1.npz), and the gradient is the identity."""
+    import os
+
+    import dscquant_b200 as dq
+
+    d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden_extra_v1.npz"))
+    x = torch.from_numpy(d["ste_x"]).to(cuda_device).requires_grad_(True)
+    y = dq.ste_round(x)
+    (y * torch.from_numpy(d["ste_w"]).to(cuda_device)).sum().backward()
+    np.testing.assert_array_equal(y.detach().cpu().numpy().view(np.uint32), d["ste_y"].view(np.uint32))
+    np.testing.assert_array_equal(x.grad.cpu().numpy(), d["ste_grad"])
+    with pytest.raises(RuntimeError):
+        dq.ste_round(torch.zeros(3))  # CUDA tensors only

@@ -131,3 +131,32 @@ def test_online_scaling_keeps_plain_up_weight(gt):
     down = QuantLinear(_lin(gt["down_w"]), cfg, interface=sc, role="down")
     assert not down.online_up_scaling
     np.testing.assert_array_equal(_bits(down.transformed()[0]), gt["down_w_t"])
+
+
+EXTRA = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden_extra_v1.npz")
+
+
+def test_transform_state_restatement_matches_reference():
+    """dscquant_b200.transforms rebuilds Rotation.matrices() and Scaling.diagonal() from an Interface's saved
+    buffers and parameters bit for bit (golden_extra_v1.npz from core/transforms.py:42-52, 71-72)."""
+    from dscquant_b200 import transforms as T
+
+    d = np.load(EXTRA)
+    st = {k: torch.from_numpy(d["rot_" + k]) for k in ("rec_basis", "sid_basis", "alpha", "beta")}
+    rot = T.RotationState(st, int(d["rot_heads"]), int(d["rot_head_dim"]))
+    np.testing.assert_array_equal(rot.matrices().numpy(), d["rot_R"])
+    R = rot.matrices().double()
+    eye = torch.eye(rot.head_dim, dtype=torch.float64).expand_as(R)
+    assert torch.allclose(R @ R.transpose(1, 2), eye, atol=1e-5)  # orthogonal per head
+    st = {k: torch.from_numpy(d["sc_" + k]) for k in ("rec_basis", "sid_basis", "alpha", "beta")}
+    np.testing.assert_array_equal(T.ScalingState(st).diagonal().numpy(), d["sc_diag"])
+    with pytest.raises(ValueError):
+        T.skew(torch.zeros(5), 1, 4)
+
+
+def test_ste_round_oracle_matches_reference(oracle):
+    """oracle.ste_round reproduces core/quantization.py:4-5 (round half to even, rounded -0 -> +0) bit for bit."""
+    d = np.load(EXTRA)
+    y = oracle.ste_round(d["ste_x"])
+    np.testing.assert_array_equal(y.view(np.uint32), d["ste_y"].view(np.uint32))
+    np.testing.assert_array_equal(d["ste_grad"], d["ste_w"])  # identity gradient in the reference
