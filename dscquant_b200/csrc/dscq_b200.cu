@@ -7,7 +7,10 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/dscq_b200.h"
@@ -226,6 +229,56 @@ cudaError_t launch_kron(const dscq::RowQuantParams& p, int a, int s, cudaStream_
   const int grid = std::min(p.rows_out, num_sms());
   dscq::kron_quant<AP><<<grid, C::THREADS, C::SMEM, st>>>(p, a, s);
   return cudaGetLastError();
+}
+
+// The tcgen05 quantizer's A operand (H'^T as the MMA reads it from shared memory) is a constant of
+// K. It is built once per (device, K) into a library-owned global buffer on the first call and kept
+// until the process exits; every launch bulk-copies it into each CTA. The first call synchronises
+// its stream and therefore cannot be part of a stream capture.
+std::mutex g_operand_mu;
+std::map<std::pair<int, int64_t>, uint8_t*> g_operands;
+
+int rotq_operand(int dev, int64_t K, const dscq::RotqParams& rp, const int8_t* h_a, cudaStream_t st,
+                 const uint8_t** out) {
+  std::lock_guard<std::mutex> lock(g_operand_mu);
+  auto it = g_operands.find({dev, K});
+  if (it != g_operands.end()) {
+    *out = it->second;
+    return DSCQ_OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(st, &cs);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+  if (cs != cudaStreamCaptureStatusNone)
+    return fail(DSCQ_ERR_UNSUPPORTED, "the first tcgen05 rotate+quantize call for K=" + std::to_string(K) +
+                                          " on a device builds its Hadamard operand and cannot be captured; make "
+                                          "one call before capturing");
+  const int a = rp.a_base;
+  if (a > 1) {  // the operand is cached by K: h_a must be the library's Hadamard factor of order a
+    std::vector<int8_t> got(static_cast<size_t>(a) * a), want(static_cast<size_t>(a) * a);
+    e = cudaMemcpyAsync(got.data(), h_a, got.size(), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "reading h_a");
+    if (!dscq::build_hadamard(a, want.data()) || got != want)
+      return fail(DSCQ_ERR_INVALID, "h_a must hold the Hadamard factor dscq_hadamard(" + std::to_string(a) + ")");
+  }
+  uint8_t* buf = nullptr;
+  e = cudaMalloc(&buf, rp.a_bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(rotate+quantize operand)");
+  const int chunks = rp.mt * 128 * rp.nkb * 8;
+  if (rp.mt == 1)
+    dscq::rotq_build_operand<1><<<(chunks + 255) / 256, 256, 0, st>>>(rp, h_a, buf);
+  else
+    dscq::rotq_build_operand<2><<<(chunks + 255) / 256, 256, 0, st>>>(rp, h_a, buf);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    cudaFree(buf);
+    return cuda_fail(e, "building the rotate+quantize operand");
+  }
+  g_operands[{dev, K}] = buf;
+  *out = buf;
+  return DSCQ_OK;
 }
 
 template <int MT, int G>
@@ -601,8 +654,12 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
       rp.tma_warp = rp.tw <= 6 ? 6 : (rp.tw == 7 ? 7 : 16);
       rp.mma_warp = rp.tw <= 6 ? 7 : (rp.tw == 7 ? 15 : 17);
     }
-    if (rp.ns < 2 || static_cast<int64_t>(rp.a_base) * rp.a_base > static_cast<int64_t>(rp.ns) * rp.stage_bytes)
-      return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize: shared memory too small");
+    if (rp.ns < 2) return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize: shared memory too small");
+    int dev = 0;
+    cudaError_t ge = cudaGetDevice(&dev);
+    if (ge != cudaSuccess) return cuda_fail(ge, "cudaGetDevice");
+    st = rotq_operand(dev, K, rp, h_a, cst, &rp.a_op);
+    if (st) return st;
     CUtensorMap tm;
     st = make_rows_map(&tm, x, M, rp.ap, ld_x, rp.ap16, rp.P);
     if (st) return st;

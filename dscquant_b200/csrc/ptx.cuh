@@ -15,6 +15,12 @@
 #ifndef DSCQ_WAIT_NS
 #define DSCQ_WAIT_NS 1000000000ull  // 1 s
 #endif
+// Waits after the first unsuccessful probe pass a suspend-time hint to mbarrier.try_wait: the warp
+// is parked until the phase completes (or the hint elapses) instead of re-polling, so waiting roles
+// do not take issue slots from the roles doing the work.
+#ifndef DSCQ_SUSPEND_NS
+#define DSCQ_SUSPEND_NS 20000u
+#endif
 
 namespace dscq {
 
@@ -70,14 +76,30 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test_suspend(uint64_t* bar, uint32_t parity) {
+#if DSCQ_SUSPEND_NS > 0
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(DSCQ_SUSPEND_NS)
+      : "memory");
+  return ok != 0;
+#else
+  return mbar_test(bar, parity);
+#endif
+}
+
 // Bounded wait for the phase with the given parity to complete. `abort_flag`
 // (shared memory, may be null) lets one timed-out role release the others.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_test(bar, parity)) return true;
-    if ((it & 255u) == 0) {
+    if (mbar_test_suspend(bar, parity)) return true;
+    if ((it & (DSCQ_SUSPEND_NS > 0 ? 7u : 255u)) == 0) {
       if (abort_flag && *abort_flag) return false;
       if (globaltimer_ns() - t0 > DSCQ_WAIT_NS) {
         raise_status(kStatusWaitTimeout);
@@ -338,6 +360,14 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, const vo
                "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
                : "memory");
 }
+// Untiled bulk copy global -> this CTA's shared memory, completing `bytes` on the local mbarrier
+// `bar` (both addresses 16-byte aligned, bytes a multiple of 16; no multicast).
+__device__ __forceinline__ void bulk_load_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 // Arrive (release at cluster scope) on an mbarrier given by a shared::cluster address.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
@@ -353,13 +383,28 @@ __device__ __forceinline__ bool mbar_test_cluster(uint64_t* bar, uint32_t parity
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ bool mbar_test_cluster_suspend(uint64_t* bar, uint32_t parity) {
+#if DSCQ_SUSPEND_NS > 0
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(DSCQ_SUSPEND_NS)
+      : "memory");
+  return ok != 0;
+#else
+  return mbar_test_cluster(bar, parity);
+#endif
+}
 // Bounded wait with cluster-scope acquire (barriers that receive remote arrivals).
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_test_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_test_cluster(bar, parity)) return true;
-    if ((it & 255u) == 0) {
+    if (mbar_test_cluster_suspend(bar, parity)) return true;
+    if ((it & (DSCQ_SUSPEND_NS > 0 ? 7u : 255u)) == 0) {
       if (abort_flag && *abort_flag) return false;
       if (globaltimer_ns() - t0 > DSCQ_WAIT_NS) {
         raise_status(kStatusWaitTimeout);

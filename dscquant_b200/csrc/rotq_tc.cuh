@@ -12,10 +12,13 @@
 //     X in shared memory as [token][i][64 c]: a k-by-MN operand whose 128-byte
 //     rows hold 64 consecutive c of one i, i.e. the canonical MN-major layout,
 //     consumed by tcgen05.mma kind::f16 without any rearrangement;
-//   * H'^T (A operand, K-major, 128 rows per M tile) is built once per CTA in
-//     shared memory. For a' <= 64 (a' = 32, 64) P = 128 / a' tokens share one
-//     MMA through a block-diagonal A (k = token*a' + i), so all 128 TMEM lanes
-//     carry data; a' in (128, 256] uses two M tiles;
+//   * H'^T (A operand, K-major, 128 rows per M tile, 128-byte swizzle) is a
+//     constant of K: rotq_build_operand writes its shared-memory image to global
+//     memory once per device and K, and every CTA copies it in with one bulk
+//     copy per 16 KB atom while the first token loads are in flight. For
+//     a' <= 64 (a' = 32, 64) P = 128 / a' tokens share one MMA through a
+//     block-diagonal A (k = token*a' + i), so all 128 TMEM lanes carry data;
+//     a' in (128, 256] uses two M tiles;
 //   * D (f32, 128 lanes x 64 columns per M tile) accumulates in TMEM, up to
 //     8 token groups in flight (512 columns);
 //   * epilogue: each thread owns one TMEM lane (one i' of one token) and its
@@ -58,7 +61,58 @@ struct RotqParams {
   int team_stride;       // team t owns warps [t * team_stride, t * team_stride + tw)
   int tma_warp, mma_warp;
   int split;             // 1: every team takes one block of each MMA group; 0: teams take whole groups
+  const uint8_t* a_op;   // global image of the A operand (a_bytes, 16-byte aligned), rotq_build_operand
 };
+
+// A operand image (exactly the shared-memory layout rotq_tc feeds to the MMA): 16-byte chunk
+// u = (row * nkb + kb) * 8 + ch holds A[row][k0 .. k0+7], k0 = kb * 64 + ch * 8, row = m * 128 + r,
+// at byte (m * nkb + kb) * 16384 + r * 128 + ((ch ^ (r & 7)) << 4). A[i'][i] = H'[i][i'] as bf16
+// +-1 (0 outside the live i, i' < a' and, for P > 1, outside the token's diagonal block), with
+// H'[i][i'] = H_a[i >> s][i' >> s] * (-1)^popc(i & i' & (2^s - 1)). One thread per chunk; runs once
+// per device and K, so it reads h_a (a x a, row-major, device memory) straight from global memory.
+template <int MT>
+__global__ void rotq_build_operand(const RotqParams rp, const int8_t* h_a, uint8_t* out) {
+  const int nkb = rp.nkb, ap = rp.ap, ap16 = rp.ap16, P = rp.P;
+  const int chunks = MT * 128 * nkb * 8;
+  const int s = rp.s_log, a = rp.a_base, msk = (1 << s) - 1;
+  for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < chunks; u += gridDim.x * blockDim.x) {
+    const int ch = u & 7, rk = u >> 3;
+    const int row = rk / nkb, kb = rk - row * nkb;
+    const int k0 = kb * 64 + ch * 8;
+    int ip, ikb;
+    bool row_live;
+    if (MT == 1 && P > 1) {
+      const int sh = rp.log2_ap16;
+      ip = row & (ap16 - 1);
+      ikb = k0 & (ap16 - 1);
+      row_live = ip < ap && (row >> sh) == (k0 >> sh);
+    } else {
+      ip = row;
+      ikb = k0;
+      row_live = ip < ap;
+    }
+    uint32_t wv[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      uint32_t half[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int i = ikb + 2 * t + e;
+        uint32_t v = 0;
+        if (row_live && i < ap) {
+          bool neg = (__popc(i & ip & msk) & 1) != 0;
+          if (a > 1 && h_a[(i >> s) * a + (ip >> s)] < 0) neg = !neg;
+          v = neg ? 0xBF80u : 0x3F80u;  // bf16 -1 / +1
+        }
+        half[e] = v;
+      }
+      wv[t] = half[0] | (half[1] << 16);
+    }
+    const int m = row >> 7, r = row & 127;
+    uint8_t* dst = out + (m * nkb + kb) * 16384 + r * 128 + ((ch ^ (r & 7)) << 4);
+    *reinterpret_cast<uint4*>(dst) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  }
+}
 
 // 64 consecutive TMEM columns of this thread's lane as 32 float2 (natural column order).
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float2 (&u)[32]) {
@@ -99,58 +153,59 @@ __device__ __forceinline__ float absmax64(const float2 (&u)[32]) {
   return fmaxf(m0, m1);
 }
 
-__device__ __forceinline__ uint32_t bfi4(uint32_t src, uint32_t base, uint32_t pos) {
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
-  asm("bfi.b32 %0, %1, %2, %3, 4;" : "=r"(d) : "r"(src), "r"(base), "r"(pos));
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
 }
 
 // Codes of 64 values -> 32 packed bytes (even k in the low nibble) at prow (if
 // not null); optional int8 codes at crow; returns the code sum when SUMS.
+// q = v * cm is rounded half to even by adding 1.5 * 2^23 (one FFMA2 per pair without clipping:
+// the fused multiply-add rounds once, so codes can differ from a separately rounded product only
+// where v * cm lies within an ulp of a .5 tie); the low byte of each result's bit pattern is then
+// the two's-complement code. Eight codes go to one word: byte-gather the even and the odd codes
+// (PRMT) and interleave their nibbles with one shift and one select (LOP3).
 template <bool SUMS, bool CLAMP>
 __device__ __forceinline__ int quant_store64(const float2 (&u)[32], float cm, float lo, uint8_t* prow, int8_t* crow) {
-  uint32_t w[8];
+  uint32_t w[8], ev[8], od[8];
   int csum = 0;
   const float2 cm2 = make_float2(cm, cm), magic = make_float2(12582912.f, 12582912.f);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    uint32_t word = 0;
+    uint32_t bx[4], by[4];
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-      float2 q = __fmul2_rn(u[4 * j + t], cm2);
-      if (CLAMP) {
+      float2 r;
+      if (CLAMP) {  // clip < 1: the scaled value may leave [lo, 7]; clamp before rounding
+        float2 q = __fmul2_rn(u[4 * j + t], cm2);
         q.x = fminf(fmaxf(q.x, lo), 7.f);
         q.y = fminf(fmaxf(q.y, lo), 7.f);
+        r = __fadd2_rn(q, magic);
+      } else {
+        r = __ffma2_rn(u[4 * j + t], cm2, magic);
       }
-      const float2 r = __fadd2_rn(q, magic);  // round half to even into the low mantissa bits
-      const uint32_t u0 = __float_as_uint(r.x), u1 = __float_as_uint(r.y);
-      word = bfi4(u0, word, 8 * t);
-      word = bfi4(u1, word, 8 * t + 4);
-      if (SUMS) csum += (static_cast<int>(u0 << 28) >> 28) + (static_cast<int>(u1 << 28) >> 28);
+      bx[t] = __float_as_uint(r.x);
+      by[t] = __float_as_uint(r.y);
+      if (SUMS) csum += (static_cast<int>(bx[t] << 28) >> 28) + (static_cast<int>(by[t] << 28) >> 28);
     }
-    w[j] = word;
+    ev[j] = prmt(prmt(bx[0], bx[1], 0x0040u), prmt(bx[2], bx[3], 0x0040u), 0x5410u);  // codes 8j, 8j+2, +4, +6
+    od[j] = prmt(prmt(by[0], by[1], 0x0040u), prmt(by[2], by[3], 0x0040u), 0x5410u);  // codes 8j+1, +3, +5, +7
+    uint32_t word;
+    asm("lop3.b32 %0, %1, %2, %3, 0xE4;" : "=r"(word) : "r"(ev[j]), "r"(od[j] << 4), "r"(0x0F0F0F0Fu));
+    w[j] = word;  // (even & 0x0F..) | ((odd << 4) & 0xF0..)
   }
   if (prow) {
     uint4* dst = reinterpret_cast<uint4*>(prow);
     dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
     dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
   }
-  if (crow) {
-    uint32_t cw[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      uint32_t x = 0;
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int c = 4 * j + t;
-        const uint32_t nib = (w[c >> 3] >> (4 * (c & 7))) & 15u;
-        x |= (static_cast<uint32_t>(static_cast<int>(nib << 28) >> 28) & 0xFFu) << (8 * t);
-      }
-      cw[j] = x;
-    }
+  if (crow) {  // the gathered bytes already are the int8 codes: interleave even and odd
     uint4* cd = reinterpret_cast<uint4*>(crow);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) cd[j] = make_uint4(cw[4 * j], cw[4 * j + 1], cw[4 * j + 2], cw[4 * j + 3]);
+    for (int j = 0; j < 4; ++j)
+      cd[j] = make_uint4(prmt(ev[2 * j], od[2 * j], 0x5140u), prmt(ev[2 * j], od[2 * j], 0x7362u),
+                         prmt(ev[2 * j + 1], od[2 * j + 1], 0x5140u), prmt(ev[2 * j + 1], od[2 * j + 1], 0x7362u));
   }
   return csum;
 }
@@ -187,7 +242,7 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
   uint64_t* tfull = bars + 2 * kRqMaxStages;
   uint64_t* tempty = tfull + S;
   uint64_t* done = tempty + S;
-  uint64_t* aready = done + 1;  // A built, staging stage free
+  uint64_t* aready = done + 1;  // A operand copied in
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aready + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* red_max = reinterpret_cast<float*>(tmem_slot + 4);        // [team][parity][8]
@@ -221,136 +276,40 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int groups = rp.groups;
   const int team = warp / rp.team_stride, idx = warp % rp.team_stride;
-  // Every warp except the TMA and MMA warps builds A while the first loads are in flight; the
-  // last B stages double as staging space for H_a and are loaded only once A is complete.
-  const bool builder = warp != rp.tma_warp && warp != rp.mma_warp;
-  const int nb = static_cast<int>(blockDim.x) - 64;
-  const int bt = static_cast<int>(threadIdx.x) - 32 * ((rp.tma_warp < warp) + (rp.mma_warp < warp));
-  const int h_stages = rp.a_base > 1 ? (rp.a_base * rp.a_base + static_cast<int>(rp.stage_bytes) - 1) /
-                                           static_cast<int>(rp.stage_bytes)
-                                     : 0;
-  const int stage_first = ns - h_stages;  // stages holding H_a until A is built
-  uint8_t* stage_h = b_base + stage_first * rp.stage_bytes;
-  if (builder) {
-    // ---- H_a^T staged in shared memory: ht[c * a + r] = H_a[r][c], so 8 consecutive k of one
-    // A row are 8 consecutive bytes.
-    // 16-byte loads, up to 8 in flight per thread before any store (a dependent byte load per
-    // entry would leave each thread waiting out the global latency a*a/nb times).
-    const int8_t* ht = nullptr;
-    if (rp.a_base > 1) {
-      const int a = rp.a_base;
-      const int total = a * a;
-      const int nvec = (reinterpret_cast<uintptr_t>(p.h_a) & 15u) == 0 ? total / 16 : 0;
-      for (int v0 = bt; v0 < nvec; v0 += 8 * nb) {
-        int4 buf[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int v = v0 + k * nb;
-          buf[k] = v < nvec ? __ldg(reinterpret_cast<const int4*>(p.h_a) + v) : make_int4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int v = v0 + k * nb;
-          if (v >= nvec) break;
-          int r = (16 * v) / a, c = 16 * v - r * a;
-          const int8_t* e = reinterpret_cast<const int8_t*>(&buf[k]);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            stage_h[c * a + r] = static_cast<uint8_t>(e[j]);
-            if (++c == a) {
-              c = 0;
-              ++r;
-            }
-          }
-        }
-      }
-      for (int i = nvec * 16 + bt; i < total; i += nb) {
-        const int r = i / a, c = i - r * a;
-        stage_h[c * a + r] = static_cast<uint8_t>(p.h_a[i]);
-      }
-      ht = reinterpret_cast<const int8_t*>(stage_h);
-    }
-    named_bar_sync(5, nb);
-    // ---- A = H'^T (K-major, 128-byte swizzle). Chunk u = (row * nkb + kb) * 8 + ch holds
-    // A[row][k0 .. k0+7], k0 = kb * 64 + ch * 8, row = m * 128 + r; A[i'][i] = H'[i][i'].
-    {
-      const int nkb = rp.nkb;
-      const int chunks = MT * 128 * nkb * 8;
-      const int s = rp.s_log, a = rp.a_base, msk = (1 << s) - 1;
-      for (int u = bt; u < chunks; u += nb) {
-        const int ch = u & 7, rk = u >> 3;
-        const int row = rk / nkb, kb = rk - row * nkb;
-        const int k0 = kb * 64 + ch * 8;
-        int ip, ikb;  // i' of the row and i of k0 inside the token block
-        bool row_live;
-        if (MT == 1 && P > 1) {
-          const int sh = rp.log2_ap16;
-          ip = row & (ap16 - 1);
-          ikb = k0 & (ap16 - 1);
-          row_live = ip < ap && (row >> sh) == (k0 >> sh);
-        } else {
-          ip = row;
-          ikb = k0;
-          row_live = ip < ap;
-        }
-        // live k of the chunk (bit j: ikb + j < a')
-        uint32_t klive = !row_live ? 0u : (ikb + 8 <= ap ? 0xFFu : (ikb >= ap ? 0u : (1u << (ap - ikb)) - 1u));
-        uint32_t neg = 0;  // bit j: H'[ikb + j][ip] < 0
-        if (klive) {
-          // Sylvester factor: ikb is a multiple of 8, so (ikb + j) & ip splits into the bits of ikb and
-          // of j: sign = parity(ikb & ip) ^ parity(j & ip & 7), the latter an 8-bit Walsh row
-          const uint32_t m7 = static_cast<uint32_t>(ip & msk & 7);
-          neg = static_cast<uint32_t>((0x963C5AF066CCAA00ull >> (8 * m7)) & 0xFFu);
-          if (__popc(ikb & ip & msk) & 1) neg ^= 0xFFu;
-          if (a > 1) {  // dense factor H_a[(ikb + j) >> s][ip >> s], read from the transposed copy ht
-            const int8_t* hrow = ht + (ip >> s) * a;
-            if (s >= 3) {  // one entry covers the 8 k of the chunk
-              if (hrow[ikb >> s] < 0) neg ^= 0xFFu;
-            } else if (s == 0 && (a & 3) == 0) {  // 8 consecutive entries, two aligned words
-              const uint32_t w0 = *reinterpret_cast<const uint32_t*>(hrow + ikb);
-              const uint32_t w1 = *reinterpret_cast<const uint32_t*>(hrow + ikb + 4);
-              const uint32_t s0 = ((w0 >> 7) & 1u) | ((w0 >> 14) & 2u) | ((w0 >> 21) & 4u) | ((w0 >> 28) & 8u);
-              const uint32_t s1 = ((w1 >> 7) & 1u) | ((w1 >> 14) & 2u) | ((w1 >> 21) & 4u) | ((w1 >> 28) & 8u);
-              neg ^= s0 | (s1 << 4);
-            } else {
-              for (int j = 0; j < 8; ++j)
-                if (ikb + j < ap) neg ^= static_cast<uint32_t>(hrow[(ikb + j) >> s] < 0) << j;
-            }
-          }
-        }
-        uint32_t wv[4];
-  #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint32_t lo = ((klive >> (2 * t)) & 1u) ? (0x3F80u | (((neg >> (2 * t)) & 1u) << 15)) : 0u;
-          const uint32_t hi = ((klive >> (2 * t + 1)) & 1u) ? (0x3F80u | (((neg >> (2 * t + 1)) & 1u) << 15)) : 0u;
-          wv[t] = lo | (hi << 16);
-        }
-        const int m = row >> 7, r = row & 127;
-        uint8_t* dst = a_base + (m * nkb + kb) * 16384 + r * 128 + ((ch ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-      }
-    }
-    fence_proxy_async_smem();  // A writes and the staging reads ordered before the async proxy
-    named_bar_sync(5, nb);
-    if (bt == 0) mbar_arrive(aready);
-  }
 
   if (warp == rp.tma_warp) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
+      // The A operand (a constant of K, prebuilt in global memory, hot in L2) in 16 KB atoms, issued
+      // after the token boxes of the first MMA group so that their DRAM reads start first.
+      const int my_blocks = groups > static_cast<int>(blockIdx.x)
+                                ? (groups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                                      static_cast<int>(gridDim.x)
+                                : 0;
+      const int op_after = min(G, my_blocks);
+      bool op_issued = false;
+      auto issue_operand = [&]() {  // exactly once per CTA
+        if (op_issued) return;
+        op_issued = true;
+        mbar_arrive_expect_tx(aready, rp.a_bytes);
+        for (uint32_t off = 0; off < rp.a_bytes; off += 16384u)
+          bulk_load_g2s(a_base + off, rp.a_op + off, 16384u, aready);
+      };
       int n = 0;
       bool ok = true;
       for (int g = blockIdx.x; g < groups; g += gridDim.x, ++n) {
+        if (n == op_after) issue_operand();
         const int s = n % ns;
-        if ((n >= stage_first && n < ns && !mbar_wait(aready, 0, abort_flag)) ||
-            (n >= ns && !mbar_wait(&empty[s], ((n / ns) & 1u) ^ 1u, abort_flag))) {
+        if (n >= ns && !mbar_wait(&empty[s], ((n / ns) & 1u) ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&full[s], rp.stage_bytes);
         tma_load_3d(b_base + s * rp.stage_bytes, &tmX, &full[s], 0, 0, g * P);
       }
-      if (!ok) {  // let the loads already issued land before the CTA can exit
+      issue_operand();  // when every block of this CTA was issued first (or none exist, or on abort)
+      if (!ok) {  // let the copies already issued land before the CTA can exit
+        mbar_wait(aready, 0, nullptr);
         for (int j = n > ns ? n - ns : 0; j < n; ++j) mbar_wait(&full[j % ns], (j / ns) & 1u, nullptr);
       }
     }

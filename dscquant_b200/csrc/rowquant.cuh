@@ -11,11 +11,14 @@
 //                 (the symmetric per-token scheme of the W4A4 path)
 //   kWeightSym    weight_codes, core/quantization.py:7-11: bound 7,
 //                 code = clamp(rn(w/scale), -7, 7); also emits per-row code sums
-//   kActAsym      quantize_rows, kernel/w4a4.cu:20-63: lo/hi include 0, times clip,
-//                 scale = max((hi-lo)/15, 1e-8), zero = clamp(rn(-lo/scale), 0, 15),
-//                 q = clamp(rn(y/scale) + zero, 0, 15), packed as (q - 8) & 15
-//   kActAsymTorch activation_codes, core/quantization.py:13-21: as kActAsym but
-//                 q = clamp(rn(y/scale + zero), 0, 15)
+//   kActAsym      quantize_rows, kernel/w4a4.cu:20-63, bit for bit as nvcc builds it for
+//                 sm_100a: lo/hi include 0 and are multiplied by clip, the range hi - lo is one
+//                 fused multiply-add fma(max, clip, -lo) (nvcc's default contraction of
+//                 maximum - minimum at :43), scale = max(range/15, 1e-8),
+//                 zero = clamp(rn(-lo/scale), 0, 15), q = clamp(rn(y/scale + zero), 0, 15)
+//                 (the zero point is added before rounding, :50), packed as (q - 8) & 15
+//   kActAsymTorch activation_codes, core/quantization.py:13-21: as kActAsym with the range
+//                 rounded as hi - lo (two products, one subtraction)
 // Rows in [M, rows_out) and columns in [K, KP) are padding and get the codes
 // the reference writes there (zero point for the asymmetric modes, 0 otherwise).
 #pragma once
@@ -87,8 +90,7 @@ __device__ __forceinline__ int quant_code(float y, float scale, int zero, int mo
   const float q = __fdiv_rn(y, scale);
   if (mode == kActSym) return max(-8, min(7, __float2int_rn(q)));
   if (mode == kWeightSym) return max(-7, min(7, __float2int_rn(q)));
-  if (mode == kActAsym) return max(0, min(15, __float2int_rn(q) + zero));
-  return max(0, min(15, __float2int_rn(__fadd_rn(q, static_cast<float>(zero)))));
+  return max(0, min(15, __float2int_rn(__fadd_rn(q, static_cast<float>(zero)))));  // both asymmetric modes
 }
 
 __device__ __forceinline__ uint32_t nibble_of(int code, int mode) {
@@ -190,7 +192,8 @@ __global__ void __launch_bounds__(T) rowquant_smem(const RowQuantParams p) {
   int zero = 0;
   if (asym) {
     const float lo = __fmul_rn(a_min, p.clip), hi = __fmul_rn(a_max, p.clip);
-    scale = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), 15.f), 1e-8f);
+    const float range = p.mode == kActAsym ? __fmaf_rn(a_max, p.clip, -lo) : __fsub_rn(hi, lo);
+    scale = fmaxf(__fdiv_rn(range, 15.f), 1e-8f);
     zero = max(0, min(15, __float2int_rn(__fdiv_rn(-lo, scale))));
   } else {
     scale = fmaxf(__fdiv_rn(__fmul_rn(a_max, p.clip), 7.f), 1e-8f);
@@ -250,7 +253,8 @@ __global__ void __launch_bounds__(T) rowquant_stream(const RowQuantParams p) {
   int zero = 0;
   if (asym) {
     const float lo = __fmul_rn(a_min, p.clip), hi = __fmul_rn(a_max, p.clip);
-    scale = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), 15.f), 1e-8f);
+    const float range = p.mode == kActAsym ? __fmaf_rn(a_max, p.clip, -lo) : __fsub_rn(hi, lo);
+    scale = fmaxf(__fdiv_rn(range, 15.f), 1e-8f);
     zero = max(0, min(15, __float2int_rn(__fdiv_rn(-lo, scale))));
   } else {
     scale = fmaxf(__fdiv_rn(__fmul_rn(a_max, p.clip), 7.f), 1e-8f);

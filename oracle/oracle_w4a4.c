@@ -8,7 +8,9 @@
  *   orc_quant_rows   per-row int4 quantizers:
  *                    ACT_SYM     scale = max(absmax*clip/7, 1e-8), clamp(rn(y/s), -8, 7)
  *                    WEIGHT_SYM  core/quantization.py:7-11 (bound 7)
- *                    ACT_ASYM    kernel/w4a4.cu:20-63 (rn(y/s) + zero, packed (q-8)&15)
+ *                    ACT_ASYM    kernel/w4a4.cu:20-63 as nvcc compiles it: scale = (max*clip -
+ *                                min*clip)/15 with the subtraction fused into one fma
+ *                                (fmaf(max, clip, -(min*clip))), q = rn(y/s + zero), packed (q-8)&15
  *                    ACT_ASYM_T  core/quantization.py:13-21 (rn(y/s + zero))
  *   orc_rotate       y = x (H_a (x) H_b) / sqrt(K) in double precision
  *   orc_gemm_s4      raw[m,n] = sum_k a_s4[m,k] b_s4[n,k]  (kernel/w4a4.cu:123-148)
@@ -71,8 +73,7 @@ static inline int code_of(float y, float scale, int zero, int mode) {
   switch (mode) {
     case ORC_ACT_SYM: return clampi(rn(q), -8, 7);
     case ORC_WEIGHT_SYM: return clampi(rn(q), -7, 7);
-    case ORC_ACT_ASYM: return clampi(rn(q) + zero, 0, 15);
-    default: {
+    default: {  /* both asymmetric modes: kernel/w4a4.cu:50 and core/quantization.py:20 round y/s + zero */
       float t = q + (float)zero;
       return clampi(rn(t), 0, 15);
     }
@@ -110,7 +111,8 @@ static void quant_range(int64_t r0, int64_t r1, void* vctx) {
     int zero = 0;
     if (asym) {
       float lo = amin * clip, hi = amax * clip;
-      scale = (hi - lo) / 15.f;
+      /* kernel/w4a4.cu:42-43: nvcc contracts maximum - minimum into fma(upper, clip, -minimum) */
+      scale = (mode == ORC_ACT_ASYM ? fmaf(amax, clip, -lo) : hi - lo) / 15.f;
       if (!(scale > 1e-8f)) scale = 1e-8f;
       zero = clampi(rn(-lo / scale), 0, 15);
     } else {
