@@ -962,3 +962,144 @@ int dscq_unpack_int4(const uint8_t* packed, int64_t rows, int64_t ld_packed, int
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ rotate+quantize without allocation
+// For callers that must not allocate device memory: serving engines that reserve all of HBM up
+// front for weights and KV cache and hand out memory only from their own pool, or latency-critical
+// paths that cannot take cudaMalloc's implicit device synchronisation. dscq_rowquant builds the
+// tcgen05 quantizer's Hadamard operand once per device and K into a buffer it allocates with
+// cudaMalloc; this variant keeps that operand in a fixed array instead, rebuilt by every call.
+
+// Largest operand of the tcgen05 quantizer: two 128-row M tiles x four 64-wide k atoms (a' <= 256).
+constexpr uint32_t kRotqScratchBytes = 128u * 1024u;
+
+// The operand scratch: one array per device, loaded with the library and held until the process
+// exits. Host code must not use this name as a device address; see rotq_scratch_address.
+static __device__ __align__(256) uint8_t g_rotq_scratch[kRotqScratchBytes];
+
+namespace {
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[64] = {};
+
+// Device address of g_rotq_scratch for device `dev` (which must be current): looked up once per
+// device with cudaGetSymbolAddress, then cached.
+int rotq_scratch_address(int dev, void** out) {
+  if (dev < 0 || dev >= 64) return fail(DSCQ_ERR_UNSUPPORTED, "device index out of range for the scratch cache");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_rotq_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(rotate+quantize scratch)");
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return DSCQ_OK;
+}
+
+}  // namespace
+
+extern "C" int dscq_rowquant_tc_noalloc(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x, int rotate,
+                                        int rot_a, const int8_t* h_a, int mode, float clip, int64_t rows_out,
+                                        int64_t KP, uint8_t* packed, int64_t ld_packed, float* scales,
+                                        int32_t* zeros, int32_t* row_sums, int8_t* codes, int64_t ld_codes,
+                                        void* stream) {
+  (void)zeros;  // symmetric modes only: no zero points
+  DSCQ_REQUIRE(x && (packed || codes) && scales, "x, scales and packed or codes must not be null");
+  DSCQ_REQUIRE(M >= 1 && M <= (1 << 24) && rows_out >= M && rows_out <= (1 << 24), "require 1 <= M <= rows_out <= 2^24");
+  DSCQ_REQUIRE(K >= 1 && K <= kMaxRotK && ld_x >= K, "require 1 <= K <= 32768 and ld_x >= K");
+  DSCQ_REQUIRE(!packed || ld_packed >= KP / 2, "ld_packed must be >= KP/2");
+  DSCQ_REQUIRE(!codes || ld_codes >= KP, "ld_codes must be >= KP");
+  DSCQ_REQUIRE(std::isfinite(clip) && clip > 0.f, "clip must be a positive finite number");
+  int log2b = 0, a = 0;
+  if (!rotate || !dscq::rotation_split(K, &a, &log2b))
+    return fail(DSCQ_ERR_UNSUPPORTED, "dscq_rowquant_tc_noalloc needs the online rotation with a supported split of K");
+  DSCQ_REQUIRE(a == rot_a && (a == 1 || h_a != nullptr), "rot_a / h_a must be the Hadamard factor of K's split");
+  const int ap = log2b >= 6 ? static_cast<int>(K / 64) : 0;
+  const bool sym = mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM;
+  if (!(ap >= 16 && ap <= 224 && sym && x_dtype == DSCQ_BF16 && KP == K && aligned(x, 16) && ld_x % 8 == 0 &&
+        (!packed || (aligned(packed, 16) && ld_packed % 16 == 0)) && (!codes || (aligned(codes, 16) && ld_codes % 16 == 0))))
+    return fail(DSCQ_ERR_UNSUPPORTED, "dscq_rowquant_tc_noalloc: needs K = a' * 64 (16 <= a' <= 224), a symmetric "
+                                      "mode, bf16 input, KP == K and 16-byte aligned rows");
+  int dev = 0;
+  int st = check_device(&dev);
+  if (st) return st;
+
+  dscq::RotqParams rp;
+  dscq::RowQuantParams& p = rp.p;
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.ld_x = ld_x;
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.KP = static_cast<int>(KP);
+  p.rows_out = static_cast<int>(rows_out);
+  p.rotate = 1;
+  p.rot_a = a;
+  p.log2b = log2b;
+  p.h_a = h_a;
+  p.norm = static_cast<float>(1.0 / std::sqrt(static_cast<double>(K)));
+  p.mode = mode;
+  p.clip = clip;
+  p.packed = packed;
+  p.ld_packed = ld_packed;
+  p.scales = scales;
+  p.zeros = nullptr;
+  p.row_sums = row_sums;
+  p.codes = codes;
+  p.ld_codes = ld_codes;
+  rp.a_base = a;
+  rp.s_log = log2b - 6;
+  rp.ap = ap;
+  rp.ap16 = (ap + 15) / 16 * 16;
+  rp.P = (rp.ap16 == 32 || rp.ap16 == 64) ? 128 / rp.ap16 : 1;
+  rp.log2_ap16 = rp.ap16 == 32 ? 5 : 6;
+  rp.mt = rp.ap16 <= 128 ? 1 : 2;
+  rp.groups = static_cast<int>((rows_out + rp.P - 1) / rp.P);
+  rp.ksteps = (rp.mt == 1 ? rp.P * rp.ap16 : rp.ap16) / 16;
+  rp.nkb = (rp.ksteps * 16 + 63) / 64;
+  rp.a_bytes = static_cast<uint32_t>(rp.mt * rp.nkb * 16384);
+  rp.stage_bytes = static_cast<uint32_t>(rp.P * rp.ap16 * 128);
+  rp.ns = std::min<int>(dscq::kRqMaxStages, (210 * 1024 - static_cast<int>(rp.a_bytes)) / static_cast<int>(rp.stage_bytes));
+  const int G = rp.mt == 1 ? 4 : 2;
+  rp.ns = rp.ns / G * G;
+  rp.split = rp.mt == 1 ? 1 : 0;
+  if (rp.mt == 1) {
+    rp.tw = 4;
+    rp.team_stride = 4;
+    rp.nteam = 4;
+    rp.tma_warp = 16;
+    rp.mma_warp = 17;
+  } else {
+    rp.tw = 4 + (rp.ap - 128 + 31) / 32;
+    rp.team_stride = 8;
+    rp.nteam = 2;
+    rp.tma_warp = rp.tw <= 6 ? 6 : (rp.tw == 7 ? 7 : 16);
+    rp.mma_warp = rp.tw <= 6 ? 7 : (rp.tw == 7 ? 15 : 17);
+  }
+  if (rp.ns < 2) return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize: shared memory too small");
+  if (rp.a_bytes > kRotqScratchBytes)
+    return fail(DSCQ_ERR_UNSUPPORTED, "K=" + std::to_string(K) + " needs " + std::to_string(rp.a_bytes) +
+                                          " bytes of operand scratch; the static scratch holds " +
+                                          std::to_string(kRotqScratchBytes));
+  void* scratch = nullptr;
+  st = rotq_scratch_address(dev, &scratch);
+  if (st) return st;
+  cudaStream_t cst = static_cast<cudaStream_t>(stream);
+  // The builder writes every byte of the operand region, so nothing left by an earlier call (of
+  // another K) survives into this one.
+  const int chunks = rp.mt * 128 * rp.nkb * 8;
+  if (rp.mt == 1)
+    dscq::rotq_build_operand<1><<<(chunks + 255) / 256, 256, 0, cst>>>(rp, h_a, static_cast<uint8_t*>(scratch));
+  else
+    dscq::rotq_build_operand<2><<<(chunks + 255) / 256, 256, 0, cst>>>(rp, h_a, static_cast<uint8_t*>(scratch));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch rotq_build_operand (static scratch)");
+  rp.a_op = static_cast<const uint8_t*>(scratch);
+  CUtensorMap tm;
+  st = make_rows_map(&tm, x, M, rp.ap, ld_x, rp.ap16, rp.P);
+  if (st) return st;
+  e = rp.mt == 1 ? launch_rotq<1, 4>(tm, rp, cst) : launch_rotq<2, 2>(tm, rp, cst);
+  if (e != cudaSuccess) return cuda_fail(e, "launch rotq_tc (static scratch)");
+  return DSCQ_OK;
+}

@@ -183,6 +183,27 @@ int dscq_matmul_cols(const uint8_t* a, const uint8_t* b, const float* sx, const 
                      int out_dtype, void* const* outs, int n_outs, int64_t ld_out, int64_t col_off, int variant,
                      void* stream);
 
+/*
+ * dscq_rowquant's tcgen05 rotate+quantize without any device allocation. No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc, such as serving engines that
+ * reserve all device memory up front for weights and KV cache and allocate only from their own
+ * pool, or latency-critical paths that cannot take cudaMalloc's implicit device synchronisation.
+ * dscq_rowquant allocates a small buffer once per device and K for the quantizer's Hadamard
+ * operand; this entry point instead rebuilds that operand on every call (one extra small launch on
+ * `stream`) into a fixed 128 KiB array that the library holds on every device it is loaded on until
+ * the process exits. Same arguments, requirements and result bits as dscq_rowquant_variant with
+ * DSCQ_QUANT_TC (rotate != 0, K = a' * 64 with 16 <= a' <= 224, DSCQ_ACT_SYM or DSCQ_WEIGHT_SYM,
+ * bf16 x, KP == K, 16-byte aligned rows; `zeros` is ignored); anything else, including an operand
+ * larger than the array, returns DSCQ_ERR_UNSUPPORTED.
+ * The first call on a device looks up the array's device address; make that first call before any
+ * stream capture. All calls on a device share the one array: calls that can overlap on the GPU
+ * (different streams without ordering between them) race and must not be issued.
+ */
+int dscq_rowquant_tc_noalloc(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld_x, int rotate, int rot_a,
+                             const int8_t* h_a, int mode, float clip, int64_t rows_out, int64_t KP, uint8_t* packed,
+                             int64_t ld_packed, float* scales, int32_t* zeros, int32_t* row_sums, int8_t* codes,
+                             int64_t ld_codes, void* stream);
+
 /* pack_int4, core/quantization.py:31-40. codes [rows, K] int8 (row stride
  * ld_codes) -> packed [rows, ceil(K/2)] (row stride ld_packed). Codes outside
  * [-8, 7] are counted into *bad_count (device int, caller-zeroed). */
