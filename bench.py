@@ -1,20 +1,23 @@
 #!/usr/bin/env python
-"""W4A4 linear benchmark on B200 (Llama-2-7B linear shapes).
+"""W4A4 linear benchmark on B200 (Llama-2-7B linear shapes), with the other configs
+as sub-records of the same JSON line.
 
-One step = the seven W4A4 linears of one Llama-2-7B decoder layer at M tokens
-(q, k, v, o: 4096 -> 4096; gate, up: 4096 -> 11008; down: 11008 -> 4096 with the
-172 x 64 Hadamard-product rotation), each one fused rotate+quantize of its
-input (shared by q/k/v and by gate/up) plus one tcgen05 W4A4 GEMM with the
-dequant epilogue: 4 + 7 kernel launches. Metric: W4A4 linear TOPS
-(2*M*N*K integer ops per linear) over the whole step.
+One step = the seven W4A4 linears of every layer of a 32-layer Llama-2-7B at M = 2048 tokens per GPU
+(q, k, v, o: 4096 -> 4096; gate, up: 4096 -> 11008; down: 11008 -> 4096 with the 172 x 64
+Hadamard-product rotation), each layer with its own weights and inputs resident in HBM: per layer one
+fused rotate+quantize per distinct input (shared by q/k/v and by gate/up) plus one tcgen05 W4A4 GEMM
+with the dequant epilogue per linear, 4 + 7 launches. Metric: W4A4 linear TOPS (2*M*N*K integer ops
+per linear) over the whole step.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 (under torchrun): every rank runs the same layer on its own token batch
-(data parallel over tokens, no collective on the data path), weak scaling;
-elapsed time is the max over ranks. `--impl reference` times the CPU W4A4
-linear of the oracle restatement (the reference's own path is PyTorch CPU
-fake-quant; its arithmetic is restated in oracle/) on the host cores.
+N > 1 (under torchrun): every rank runs the step on its own token batch (data parallel over tokens, no
+collective on the data path), weak scaling; elapsed time is the max over ranks. At every N the line
+also carries `config4_tp`: the Llama-2-70B layer linears split column-parallel over the N ranks
+(strong scaling) with the fused NVLink exchange and the NCCL all-gather, per-phase times included.
+At N = 1 rank 0 adds the kernel sweeps of configs 1 and 3, the config-2 prefill and the CPU
+baseline. `--impl reference` times the reference's own CPU path (QuantLinear.forward as shipped,
+restated bit-exactly in oracle/oracle_torch.py) on the host cores on the same workload.
 """
 from __future__ import annotations
 
@@ -41,15 +44,13 @@ METRIC = "W4A4 linear TOPS at Llama-2-7B shapes (M=1..2048), % of int8 TC peak"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "llama2-70b-tp"],
-                   help="llama2-7b: config 1 layer, data parallel over tokens (default); "
-                        "llama2-70b-tp: config 4 layer, column-parallel over N with the fused all-gather")
-    p.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"])
     p.add_argument("--tokens", type=int, default=2048)
-    p.add_argument("--replicas", type=int, default=4, help="layer replicas cycled so the working set exceeds L2")
+    p.add_argument("--layers", type=int, default=32, help="distinct Llama-2-7B layers per step (32: the whole model)")
+    p.add_argument("--no-tp", action="store_true", help="skip the config-4 column-parallel record")
+    p.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill record")
     p.add_argument("--activations", default="packed", choices=["packed", "int8"],
                    help="activation codes handed from the quantizer to the GEMM: packed nibbles (dscq_matmul, "
                         "the reference's format) or one int8 code per element (dscq_matmul_a8); same result bits")
@@ -371,76 +372,254 @@ def run_reference(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-# ---------------------------------------------------------------- config 4: column-parallel 70B layer
+# ---------------------------------------------------------------- synthetic model state on the GPU
+LAYER3 = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
+          ("gate", 4096, 14336), ("up", 4096, 14336), ("down", 14336, 4096)]
+INPUT_K3 = {"attn": 4096, "o": 4096, "mlp": 4096, "down": 14336}
 LAYER70 = [("qkv", 8192, 10240), ("o", 8192, 8192), ("gate", 8192, 28672), ("up", 8192, 28672), ("down", 28672, 8192)]
+DATA = "synthetic (seeded N(0,1) activations with 1% x20 outlier channels, N(0,0.02) weights, generated on the GPU)"
 
 
-def run_tp(args) -> None:
-    """Llama-2-70B layer linears at M = 4096 tokens, column-parallel over N on every
-    rank of the job; the shards are exchanged inside the GEMM epilogue (fused) or by NCCL all-gather.
-    Strong scaling: the total work is fixed; value = layer ops / max-over-ranks step time."""
-    import datetime
+def activations_gpu(M: int, K: int, gen, dev):
+    """[M, K] bf16 ~ N(0, 1) with 1% of the K channels (seeded choice) scaled x20: the benchmark distribution."""
+    import torch
+
+    x = torch.randn(M, K, generator=gen, device=dev)
+    cols = torch.randperm(K, generator=gen, device=dev)[: max(1, K // 100)]
+    x[:, cols] *= 20.0
+    return x.to(torch.bfloat16)
+
+
+class Quant:
+    """Preallocated outputs of one rotate+quantize launch (C ABI, the AUTO kernel) for a [M, K] input."""
+
+    def __init__(self, M: int, K: int, dev, a8: bool = False):
+        import torch
+
+        from dscquant_b200 import ops
+
+        self.M, self.K, self.a8 = M, K, a8
+        self.packed = None if a8 else torch.empty((M, K // 2), dtype=torch.uint8, device=dev)
+        self.codes = torch.empty((M, K), dtype=torch.int8, device=dev) if a8 else None
+        self.scales = torch.empty((M,), dtype=torch.float32, device=dev)
+        self.rot_a, self.h = ops.rotation_factor(K, dev)
+        self.dev = dev
+
+    def __call__(self, x):
+        from dscquant_b200 import _lib, ops
+
+        rc = _lib.load().dscq_rowquant(ops._ptr(x), _lib.BF16, self.M, self.K, x.stride(0), 1, self.rot_a,
+                                       ops._ptr(self.h), _lib.ACT_SYM, 1.0, self.M, self.K, ops._ptr(self.packed),
+                                       0 if self.a8 else self.K // 2, ops._ptr(self.scales), None, None,
+                                       ops._ptr(self.codes), self.K if self.a8 else 0, ops._stream(self.dev))
+        _lib.check(rc, "rowquant")
+
+
+def gemm_call(q: Quant, mod, out, M: int, N: int, K: int, dev):
+    from dscquant_b200 import _lib, ops
+
+    p = mod._prep
+    if q.a8:
+        rc = _lib.load().dscq_matmul_a8(ops._ptr(q.codes), K, ops._ptr(p["packed"]), ops._ptr(q.scales),
+                                        ops._ptr(p["sw"]), None, None, M, N, K, _lib.BF16, ops._ptr(out), None,
+                                        ops._stream(dev))
+    else:
+        rc = _lib.load().dscq_matmul(ops._ptr(q.packed), ops._ptr(p["packed"]), ops._ptr(q.scales), None,
+                                     ops._ptr(p["sw"]), None, None, None, M, N, K, _lib.BF16, ops._ptr(out), None, 0,
+                                     ops._stream(dev))
+    _lib.check(rc, "matmul")
+
+
+# ---------------------------------------------------------------- kernel-level sweep (configs 1 and 3)
+def sweep_shapes(shapes, Ms, dev, peaks, gen):
+    """rotate+quantize and GEMM of each (K, N) at each M, timed per launch with CUDA events, L2 flushed
+    (512 MB written) before every timed call; median of 6 after 2 untimed."""
+    import statistics
 
     import torch
-    import torch.distributed as tdist
 
-    from dscquant_b200 import _lib, ops, parallel, synthetic  # noqa: F401
+    from dscquant_b200 import ops
+    from dscquant_b200.llama import random_quant_linear
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ.setdefault("MASTER_PORT", "29531")
-    tdist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                             device_id=dev)
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    out = []
+    for (K, N) in shapes:
+        ql = random_quant_linear(N, K, gen, dev)
+        for m in Ms:
+            x = activations_gpu(m, K, gen, dev)
+            g_t, q_t = [], []
+            for it in range(8):
+                flush.zero_()
+                e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                e[0].record(stream)
+                q = ops.rowquant(x, "act_sym", rotate=True, KP=K)
+                e[1].record(stream)
+                ops.w4a4_gemm(q.packed, ql._prep["packed"], q.scales, ql._prep["sw"], M=m, N=N)
+                e[2].record(stream)
+                torch.cuda.synchronize(dev)
+                if it >= 2:
+                    q_t.append(e[0].elapsed_time(e[1]))
+                    g_t.append(e[1].elapsed_time(e[2]))
+            gm, qm = statistics.median(g_t), statistics.median(q_t)
+            ops_ = 2.0 * m * N * K
+            gbytes = m * K / 2 + N * K / 2 + 2 * m * N + 4 * m + 4 * N
+            out.append({"M": m, "K": K, "N": N, "gemm_us": round(gm * 1e3, 2), "quant_us": round(qm * 1e3, 2),
+                        "gemm_tops": round(ops_ / (gm * 1e-3) / 1e12, 1),
+                        "linear_tops": round(ops_ / ((gm + qm) * 1e-3) / 1e12, 1),
+                        "gemm_frac_int8_peak": round(ops_ / (gm * 1e-3) / 1e12 / int8_peak, 3),
+                        "gemm_frac_hbm": round(gbytes / (gm * 1e-3) / 1e9 / peaks["hbm_gbs"], 3),
+                        "quant_frac_hbm": round((m * K * 2.5 + 4 * m) / (qm * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)})
+        del ql
+    del flush
+    return out
+
+
+def layer_from_sweep(sweep, layer, input_k):
+    """Per-M layer figures from the sweep: every GEMM of the layer plus one rotate+quantize per distinct
+    input (q/k/v share one, gate/up share one)."""
+    res = {}
+    for m in sorted({r["M"] for r in sweep}):
+        rows = {(r["K"], r["N"]): r for r in sweep if r["M"] == m}
+        gemm_us = sum(rows[(k, n)]["gemm_us"] for _, k, n in layer)
+        quant_us = sum(next(r["quant_us"] for (kk, _), r in rows.items() if kk == K) for K in input_k.values())
+        ops_ = sum(2.0 * m * n * k for _, k, n in layer)
+        res[str(m)] = {"layer_tops": round(ops_ / ((gemm_us + quant_us) * 1e-6) / 1e12, 1),
+                       "gemm_tops": round(ops_ / (gemm_us * 1e-6) / 1e12, 1),
+                       "gemm_us": round(gemm_us, 2), "quant_us": round(quant_us, 2)}
+    return res
+
+
+# ---------------------------------------------------------------- config 4: Llama-2-70B layer, column-parallel
+def tp70_record(dev, rank: int, world: int, steps: int = 10, warmup: int = 3) -> dict:
+    """The five Llama-2-70B layer linears at M = 4096, output channels split over the `world` ranks of the
+    job (strong scaling: the total work is fixed). N = 1: one GPU, no exchange. N > 1: both exchange modes
+    of parallel.ColumnParallelQuantLinear -- 'fused' (row-split quantisation into symmetric memory, peer
+    reads of the other ranks' rows, GEMM epilogue storing every tile into every rank's output over
+    NVLink) and 'nccl' (replicated quantisation, local GEMM, NCCL all-gather, reassembly). Times are CUDA
+    events on each rank's stream, max over ranks; per-phase milliseconds per step from events recorded
+    at the phase boundaries of every call (max over ranks)."""
+    import torch
+
+    from dscquant_b200 import ops, parallel
+    from dscquant_b200.llama import random_quant_linear
+
     M = 4096
+    ops_total = float(sum(2 * M * n * k for _, k, n in LAYER70))
     gen = torch.Generator(device=dev)
-    layers = []
-    for i, (name, K, N) in enumerate(LAYER70):
-        lo, hi = parallel.shard_bounds(N, world, rank)
-        gen.manual_seed(7000 + 31 * i + rank)
-        w = (torch.randn((hi - lo, K), generator=gen, device=dev, dtype=torch.float32) * 0.02).to(torch.bfloat16)
-        layers.append((name, K, N, parallel.ColumnParallelQuantLinear(w, N, mode=args.tp_mode, max_tokens=M)))
-        del w
+    stream = torch.cuda.current_stream(dev)
     xs = {}
     for K in sorted({k for _, k, _ in LAYER70}):
         gen.manual_seed(9000 + K)
-        xs[K] = torch.randn((M, K), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    stream = torch.cuda.current_stream(dev)
+        xs[K] = activations_gpu(M, K, gen, dev)
 
-    def step():
-        for name, K, N, layer in layers:
-            layer(xs[K])
+    def timed(step):
+        for _ in range(warmup):
+            step()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
 
-    for _ in range(max(args.warmup, 1)):
-        step()
-    tdist.barrier()
+    rec = {"workload": "llama2-70b-layer-linears", "tokens": M, "shapes_KxN": [[k, n] for _, k, n in LAYER70],
+           "n_gpus": world, "scaling": "strong", "unit": "TOPS"}
+    if world == 1:
+        mods = []
+        for i, (name, K, N) in enumerate(LAYER70):
+            gen.manual_seed(7000 + 31 * i)
+            mods.append((K, N, random_quant_linear(N, K, gen, dev)))
+
+        def step():
+            for K, N, ql in mods:
+                q = ops.rowquant(xs[K], "act_sym", rotate=True, KP=K)
+                ops.w4a4_gemm(q.packed, ql._prep["packed"], q.scales, ql._prep["sw"], M=M, N=N)
+
+        ms = timed(step)
+        rec["single"] = {"ms_per_step": ms, "value": ops_total / (ms * 1e-3) / 1e12}
+        rec["value"] = rec["single"]["value"]
+        return rec
+    for mode in ("fused", "nccl"):
+        layers = []
+        for i, (name, K, N) in enumerate(LAYER70):
+            lo, hi = parallel.shard_bounds(N, world, rank)
+            gen.manual_seed(7000 + 31 * i)
+            w = (torch.randn((N, K), generator=gen, device=dev) * 0.02).to(torch.bfloat16)[lo:hi].contiguous()
+            layers.append((K, parallel.ColumnParallelQuantLinear(w, N, mode=mode, max_tokens=M, copy_out=False)))
+            del w
+
+        def step():
+            for K, layer in layers:
+                layer(xs[K])
+
+        ms = timed(step)
+        # phase breakdown: one more instrumented pass of `steps` steps
+        for _, layer in layers:
+            layer.timeline = []
+        for _ in range(steps):
+            step()
+        torch.cuda.synchronize(dev)
+        phases = {}
+        for _, layer in layers:
+            tl = layer.timeline
+            for (_, a), (name, b) in zip(tl[:-1], tl[1:]):
+                if name == "start":
+                    continue
+                phases[name] = phases.get(name, 0.0) + a.elapsed_time(b)
+            layer.timeline = None
+        names = sorted(phases)
+        t = torch.tensor([phases[n] / steps for n in names], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        rec[mode] = {"ms_per_step": ms, "value": ops_total / (ms * 1e-3) / 1e12,
+                     "phase_ms_per_step": {n: round(float(v), 4) for n, v in zip(names, t.tolist())}}
+        del layers
+        torch.cuda.synchronize(dev)
+        torch.distributed.barrier()
+    rec["value"] = max(rec["fused"]["value"], rec["nccl"]["value"])
+    return rec
+
+
+# ---------------------------------------------------------------- config 2: Llama-2-7B prefill
+def prefill_record(dev, seq: int = 2048, reps: int = 5) -> dict:
+    import torch
+
+    from dscquant_b200.llama import LlamaConfig, LlamaW4A4
+
+    cfg = LlamaConfig()
+    model = LlamaW4A4(cfg, dev, seed=11)
+    ids = torch.randint(0, cfg.vocab, (seq,), device=dev, generator=torch.Generator(device=dev).manual_seed(12))
+    for _ in range(2):
+        model(ids)
     torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        step()
+    for _ in range(reps):
+        logits = model(ids)
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
-    ms = float(t.item())
-    ops_ = float(sum(2 * M * n * k for _, k, n in LAYER70))
-    if rank == 0:
-        print(json.dumps({"metric": "W4A4 linear TOPS, Llama-2-70B layer linears, column-parallel over N",
-                          "value": ops_ / (ms * 1e-3) / 1e12, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
-                          "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-                          "vs_baseline": None, "dtype": "int4 x int4 -> int32 (bf16 in/out)",
-                          "data": "synthetic (seeded normal activations and weights)",
-                          "config": {"workload": "llama2-70b-tp", "tokens": M, "tp_mode": args.tp_mode,
-                                     "shapes_KxN": [[k, n] for _, k, n in LAYER70],
-                                     "parallelism": f"tp{world} column-parallel over N"}}), flush=True)
-    del layers
-    tdist.barrier()
-    tdist.destroy_process_group()
+    ms = e0.elapsed_time(e1) / reps
+    ok = bool(torch.isfinite(logits.float()).all())
+    rec = {"workload": "llama2-7b-prefill", "batch": 1, "seq_len": seq, "layers": cfg.layers, "vocab": cfg.vocab,
+           "tokens_per_s": seq / (ms * 1e-3), "ms_per_prefill": ms, "reps": reps,
+           "w4a4_linear_tops": model.linear_ops(seq) / (ms * 1e-3) / 1e12, "logits_finite": ok,
+           "note": "all 224 projections + LM head W4A4 (rotate+quantize shared by q/k/v and by gate/up, residuals "
+                   "added in the GEMM epilogue); attention bf16 torch SDPA; RMSNorm / RoPE / SiLU torch ops; "
+                   "random-init weights, uniform random token ids"}
+    del model
+    torch.cuda.empty_cache()
+    return rec
 
 
 # ---------------------------------------------------------------- GPU arm
@@ -453,20 +632,14 @@ def main():
     if args.kernel_case:
         kernel_case(args)
         return
-    if args.workload == "llama2-70b-tp" and args.impl == "ours":
-        run_tp(args)
-        return
     if args.impl == "reference":
-        if dist:
-            pass  # other ranks exit without work
-        run_reference(args, rank, world)
+        run_reference(args, rank, world)  # rank 0 runs, other ranks exit without work
         return
 
-    import numpy as np
     import torch
 
-    import dscquant_b200 as dq
-    from dscquant_b200 import _lib, ops, synthetic
+    from dscquant_b200 import _lib, ops
+    from dscquant_b200.llama import random_quant_linear
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -478,85 +651,62 @@ def main():
 
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = tdist
+    world = pg.get_world_size() if pg is not None else 1
     _lib.load()
     peaks = load_peaks()
-    M, R = args.tokens, args.replicas
-
-    # ---- model state: R replicas of one layer's weights (packed once) and inputs
-    def bf(bits):
-        return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).to(dev)
-
-    reps = []
-    for r in range(R):
-        mods = {}
-        for i, (name, K, N) in enumerate(LAYER):
-            base = torch.nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=dev)
-            with torch.no_grad():
-                base.weight.copy_(bf(synthetic.weights_bf16(N, K, seed=1000 + i + 17 * r)))
-            ql = dq.QuantLinear(base, dq.QuantConfig())
-            ql.enabled = True
-            ql.prepare()
-            ql.base.weight.data = torch.empty(0, device=dev, dtype=torch.bfloat16)  # only packed weights stay
-            mods[name] = ql
-        xs = {k: bf(synthetic.activations_bf16(M, K, seed=3000 + 31 * r + K + rank)) for k, K in INPUT_K.items()}
-        reps.append((mods, xs))
-    outs = {name: torch.empty((M, N), dtype=torch.bfloat16, device=dev) for name, _, N in LAYER}
-
+    M, L = args.tokens, args.layers
     a8 = args.activations == "int8"
-    stream = torch.cuda.current_stream(dev)
-    gemm_events = []  # (start, end, ops) of GEMM launches in the timed region
-    quant_events = []  # (start, end, bytes)
 
-    def step(i, record=False):
-        mods, xs = reps[i % R]
-        qs = {}
-        for key, K in INPUT_K.items():
-            if record:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-            qs[key] = ops.rowquant(xs[key], "act_sym", rotate=True, KP=K, codes=a8, packed_out=not a8)
-            if record:
-                e1 = torch.cuda.Event(enable_timing=True)
-                e1.record(stream)
-                quant_events.append((e0, e1, M * K * 2 + (M * K if a8 else M * K // 2) + 4 * M))
-        for name, K, N in LAYER:
-            ql = mods[name]
-            q = qs[INPUT_OF[name]]
-            p = ql._prep
-            if record:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-            if a8:
-                rc = _lib.load().dscq_matmul_a8(ops._ptr(q.codes), K, ops._ptr(p["packed"]), ops._ptr(q.scales),
-                                                ops._ptr(p["sw"]), None, None, M, N, K, _lib.BF16,
-                                                ops._ptr(outs[name]), None, ops._stream(dev))
-            else:
-                rc = _lib.load().dscq_matmul(ops._ptr(q.packed), ops._ptr(p["packed"]), ops._ptr(q.scales), None,
-                                             ops._ptr(p["sw"]), None, None, None, M, N, K, _lib.BF16,
-                                             ops._ptr(outs[name]), None, 0, ops._stream(dev))
-            _lib.check(rc, "matmul")
-            if record:
-                e1 = torch.cuda.Event(enable_timing=True)
-                e1.record(stream)
-                gemm_events.append((e0, e1, 2.0 * M * N * K))
+    # ---- model state: L distinct layers (packed weights) and their inputs, all resident in HBM
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    layers = []
+    for li in range(L):
+        mods = {name: random_quant_linear(N, K, gen, dev) for name, K, N in LAYER}
+        xs = {key: activations_gpu(M, K, gen, dev) for key, K in INPUT_K.items()}
+        layers.append((mods, xs))
+    quants = {key: Quant(M, K, dev, a8) for key, K in INPUT_K.items()}
+    outs = {name: torch.empty((M, N), dtype=torch.bfloat16, device=dev) for name, _, N in LAYER}
+    stream = torch.cuda.current_stream(dev)
+    gemm_events, quant_events = [], []
+
+    def step(record=False):
+        for mods, xs in layers:
+            for key, K in INPUT_K.items():
+                if record:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                quants[key](xs[key])
+                if record:
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e1.record(stream)
+                    quant_events.append((e0, e1, M * K * 2 + (M * K if a8 else M * K // 2) + 4 * M))
+            for name, K, N in LAYER:
+                if record:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                gemm_call(quants[INPUT_OF[name]], mods[name], outs[name], M, N, K, dev)
+                if record:
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e1.record(stream)
+                    gemm_events.append((e0, e1, 2.0 * M * N * K))
 
     def barrier():
         if pg is not None:
             pg.barrier()
         torch.cuda.synchronize(dev)
 
-    for i in range(args.warmup):
-        step(i)
+    for _ in range(args.warmup):
+        step()
     barrier()
     sampler = ClockSampler(local)
     time.sleep(0.3)
     barrier()
     t_start = time.time()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for i in range(args.steps):
-        step(i, record=True)
+    for _ in range(args.steps):
+        step(record=True)
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     t_end = time.time()
@@ -569,135 +719,118 @@ def main():
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         elapsed_ms = float(t.item())
     ms_per_step = elapsed_ms / args.steps
-    value = layer_ops(M) * world / (ms_per_step * 1e-3) / 1e12
-
+    step_ops = layer_ops(M) * L
+    value = step_ops * world / (ms_per_step * 1e-3) / 1e12
     gemm_ms = sum(a.elapsed_time(b) for a, b, _ in gemm_events)
-    gemm_ops = sum(o for _, _, o in gemm_events)
+    gemm_tops = sum(o for _, _, o in gemm_events) / (gemm_ms * 1e-3) / 1e12
     quant_ms = sum(a.elapsed_time(b) for a, b, _ in quant_events)
-    quant_bytes = sum(o for _, _, o in quant_events)
-    gemm_tops = gemm_ops / (gemm_ms * 1e-3) / 1e12
-    quant_gbs = quant_bytes / (quant_ms * 1e-3) / 1e9
-    int8_peak = 2.0 * peaks["bf16_tflops"]  # kind::i8 issues at twice the kind::f16 rate
-
+    quant_gbs = sum(o for _, _, o in quant_events) / (quant_ms * 1e-3) / 1e9
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    # the 2-SM tcgen05 int8 MMA rate measured on B200 (8176 MAC/clk/SM, cta_group::2 M=256 N=256) at the
+    # SM clock sampled during the timed region
+    mma_i8_peak = 2 * 8176 * 148 * sm_mhz * 1e6 / 1e12
     status = ops.device_status(dev)
+    del gemm_events[:], quant_events[:]
 
-    # ---- e2e through the public API (QuantLinear.forward) with pinned host buffers
-    mods = reps[0][0]
-    # one pinned host input per distinct layer input (q/k/v share one, gate/up another), copied once
-    host_in = {key: torch.empty((M, K), dtype=torch.bfloat16, pin_memory=True) for key, K in INPUT_K.items()}
-    host_out = {name: torch.empty((M, N), dtype=torch.bfloat16, pin_memory=True) for name, _, N in LAYER}
-    for key in INPUT_K:
-        host_in[key].copy_(reps[0][1][key].cpu())
-    h2d = sum(M * K * 2 for K in INPUT_K.values())
-    d2h = sum(M * N * 2 for _, _, N in LAYER)
+    # ---- e2e through the public API (QuantLinear.forward via HostPipeline) with pinned host buffers:
+    # layer 0's seven linears; median of 5 repeats
     from dscquant_b200.hostio import HostPipeline
 
+    mods0, xs0 = layers[0]
+    host_in = {key: xs0[key].cpu().pin_memory() for key in INPUT_K}
+    host_out = {name: torch.empty((M, N), dtype=torch.bfloat16, pin_memory=True) for name, _, N in LAYER}
+    h2d = sum(M * K * 2 for K in INPUT_K.values())
+    d2h = sum(M * N * 2 for _, _, N in LAYER)
     pipe = HostPipeline(dev)
     for name, _, _ in LAYER:
-        mods[name].int8_activations = a8  # same activation format as the device-resident step
-    e2e_mods = [mods[name] for name, _, _ in LAYER]
+        mods0[name].int8_activations = a8
+    e2e_mods = [mods0[name] for name, _, _ in LAYER]
     e2e_in = [host_in[INPUT_OF[name]] for name, _, _ in LAYER]
     e2e_out = [host_out[name] for name, _, _ in LAYER]
-
-    def e2e_step():
-        pipe.run(e2e_mods, e2e_in, e2e_out)
-
-    e2e_steps = max(5, min(args.steps, 30))
     for _ in range(3):
-        e2e_step()
+        pipe.run(e2e_mods, e2e_in, e2e_out)
     barrier()
-    a0 = torch.cuda.Event(enable_timing=True)
-    a1 = torch.cuda.Event(enable_timing=True)
-    a0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    stream.wait_event(pipe.done_event)
-    a1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = a0.elapsed_time(a1) / e2e_steps
+    reps = []
+    for _ in range(5):
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(10):
+            pipe.run(e2e_mods, e2e_in, e2e_out)
+        stream.wait_event(pipe.done_event)
+        a1.record(stream)
+        torch.cuda.synchronize(dev)
+        reps.append(a0.elapsed_time(a1) / 10)
+    e2e_ms = sorted(reps)[len(reps) // 2]
     if pg is not None:
         t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e_value = layer_ops(M) * world / (e2e_ms * 1e-3) / 1e12
+    del layers, quants, outs
+    torch.cuda.empty_cache()
 
-    # ---- sweep over M for the three shapes (kernel-level, L2 flushed before each timed call)
-    sweep = []
-    if not args.no_sweep and rank == 0:
-        flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
-        for (K, N) in ((4096, 4096), (4096, 11008), (11008, 4096)):
-            base = torch.nn.Linear(K, N, bias=False, dtype=torch.bfloat16, device=dev)
-            with torch.no_grad():
-                base.weight.copy_(bf(synthetic.weights_bf16(N, K, seed=K + N)))
-            ql = dq.QuantLinear(base, dq.QuantConfig())
-            ql.enabled = True
-            ql.prepare()
-            for m in (1, 16, 128, 512, 2048, 8192):
-                x = bf(synthetic.activations_bf16(m, K, seed=m))
-                g_t, q_t = [], []
-                for it in range(8):
-                    flush.zero_()
-                    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-                    e[0].record(stream)
-                    q = ops.rowquant(x, "act_sym", rotate=True, KP=K)
-                    e[1].record(stream)
-                    ops.w4a4_gemm(q.packed, ql._prep["packed"], q.scales, ql._prep["sw"], M=m, N=N)
-                    e[2].record(stream)
-                    torch.cuda.synchronize(dev)
-                    if it >= 2:
-                        q_t.append(e[0].elapsed_time(e[1]))
-                        g_t.append(e[1].elapsed_time(e[2]))
-                gm, qm = statistics.median(g_t), statistics.median(q_t)
-                ops_ = 2.0 * m * N * K
-                gbytes = m * K / 2 + N * K / 2 + 2 * m * N + 4 * m + 4 * N
-                sweep.append({"M": m, "K": K, "N": N, "gemm_us": round(gm * 1e3, 2), "quant_us": round(qm * 1e3, 2),
-                              "gemm_tops": round(ops_ / (gm * 1e-3) / 1e12, 1),
-                              "linear_tops": round(ops_ / ((gm + qm) * 1e-3) / 1e12, 1),
-                              "gemm_frac_int8_peak": round(ops_ / (gm * 1e-3) / 1e12 / int8_peak, 3),
-                              "gemm_frac_hbm": round(gbytes / (gm * 1e-3) / 1e9 / peaks["hbm_gbs"], 3),
-                              "quant_frac_hbm": round((m * K * 2.5 + 4 * m) / (qm * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)})
-        del flush
+    # ---- config 4 at this world size (every rank takes part)
+    tp = None
+    if not args.no_tp:
+        tp = tp70_record(dev, rank, world)
 
-    # ---- CPU baseline (rank 0 at N = 1)
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline_record(M)
-
-    # DRAM bytes per GEMM launch from one ncu capture of each benchmark shape at M = 2048
-    # (dram__bytes_read.sum + dram__bytes_write.sum), launch-weighted over the step's 7 GEMMs
-    gemm_kernel = "w4a4_gemm_pair_a8" if a8 else "w4a4_gemm_pair"
-    traffic = None
-    if M == 2048 and not a8:
-        per_shape = {(4096, 4096): 12.662e6, (4096, 11008): 26.866e6, (11008, 4096): 33.891e6}
-        traffic = sum(per_shape[(k, n)] for _, k, n in LAYER) / len(LAYER)
+    # ---- rank 0 extras at N = 1: kernel sweeps (configs 1 and 3), prefill (config 2), CPU baseline
+    sweep7 = sweep3 = prefill = cpu = None
+    if rank == 0 and world == 1:
+        sgen = torch.Generator(device=dev)
+        sgen.manual_seed(77)
+        if not args.no_sweep:
+            sweep7 = sweep_shapes(((4096, 4096), (4096, 11008), (11008, 4096)), (1, 16, 128, 512, 2048, 8192), dev,
+                                  peaks, sgen)
+            sweep3 = sweep_shapes(((4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)), (1, 128, 2048, 8192),
+                                  dev, peaks, sgen)
+        if not args.no_prefill:
+            prefill = prefill_record(dev)
+        if not args.no_cpu:
+            cpu = cpu_baseline_record(M)
 
     if rank == 0:
+        gemm_kernel = "w4a4_gemm_pair_a8" if a8 else "w4a4_gemm_pair"
         line = {
             "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int4 x int4 -> int32 (bf16 in/out)",
-            "data": "synthetic (seeded N(0,1) activations with 1% x20 outlier channels, N(0,0.02) weights)",
-            "config": {"workload": "llama2-7b-layer-linears", "tokens_per_gpu": M,
+            "vs_baseline": None, "dtype": "int4 x int4 -> int32 (bf16 in/out)", "data": DATA,
+            "config": {"workload": "llama2-7b-linears", "layers": L, "tokens_per_gpu": M,
                        "shapes_KxN": [[k, n] for _, k, n in LAYER], "rotation": "WHT-4096 / H172xH64 (K=11008)",
                        "activation_quant": "symmetric per-token int4", "weight_quant": "symmetric per-channel int4",
                        "activation_codes": "int8 (one code per byte)" if a8 else "packed int4 nibbles",
                        "parallelism": f"dp{world} over tokens" if world > 1 else "single GPU",
-                       "l2": f"{R} layer replicas cycled (working set > 126 MB L2)"},
-            "gpu_launches": 11 * args.steps,
+                       "l2": f"{L} distinct layers per step ({L * 101} MB of packed weights, inputs per layer): "
+                             "larger than the 126 MB L2"},
+            "gpu_launches": 11 * L * args.steps,
             "roofline": {"kernel": gemm_kernel, "bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
-                         "unit": "TFLOP/s", "frac": gemm_tops / int8_peak, "traffic": traffic,
-                         "traffic_note": f"{gemm_kernel} bytes per launch, ncu capture of each shape at M=2048 (profiles/)",
+                         "unit": "TFLOP/s", "frac": gemm_tops / int8_peak,
                          "peak_note": f"int8 dense = 2 x {peaks['source']} bf16 cuBLAS {peaks['bf16_tflops']} TFLOP/s; "
                                       "ops are integer ops (2 per MAC)",
+                         "frac_of_mma_i8_rate": gemm_tops / mma_i8_peak, "mma_i8_rate": mma_i8_peak,
+                         "mma_i8_note": "2-SM tcgen05 kind::i8 issue rate measured on B200 (8176 MAC/clk/SM) x 148 SMs "
+                                        "x the sampled SM clock",
+                         "traffic": 19.753e6 if (M == 2048 and not a8) else None,
+                         "traffic_source": "copied from an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum, "
+                                           "w4a4_gemm_pair at M=2048 on the three shapes, launch-weighted), "
+                                           "profiles/w4a4_gemm_persistent__dram_traffic_M2048.md; not measured in "
+                                           "this run",
                          "share_of_step": gemm_ms / elapsed_ms},
-            "roofline_quantize": {"kernel": "rowquant", "bound": "hbm", "achieved": quant_gbs, "peak": peaks["hbm_gbs"],
+            "roofline_quantize": {"kernel": "rotq_tc", "bound": "hbm", "achieved": quant_gbs, "peak": peaks["hbm_gbs"],
                                   "unit": "GB/s", "frac": quant_gbs / peaks["hbm_gbs"],
                                   "share_of_step": quant_ms / elapsed_ms},
             "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "HostPipeline.run over the 7 QuantLinear modules: pinned host input -> device -> "
-                           "QuantLinear.forward -> pinned host output per linear, copies in both directions "
-                           "overlapped with the kernels on three streams"},
-            "cpu_baseline": cpu, "clocks": clocks, "device_status": status, "sweep": sweep,
+                    "repeats_ms": [round(r, 3) for r in reps],
+                    "api": "HostPipeline.run over one layer's 7 QuantLinear modules: pinned host input -> device -> "
+                           "QuantLinear.forward -> pinned host output per linear, copies overlapped with the kernels "
+                           "on three streams; median of 5 repeats of 10 calls"},
+            "cpu_baseline": cpu, "clocks": clocks, "device_status": status,
+            "config4_tp": tp, "config2_prefill": prefill,
+            "config1_sweep": sweep7,
+            "config3_sweep": sweep3,
+            "config3_layer": layer_from_sweep(sweep3, LAYER3, INPUT_K3) if sweep3 else None,
+            "config1_layer": layer_from_sweep(sweep7, LAYER, INPUT_K) if sweep7 else None,
         }
         print(json.dumps(line), flush=True)
     if pg is not None:

@@ -414,13 +414,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // ------------------------------------------------ epilogue
   const int row_local = warp * 32 + lane;  // TMEM lane == tile row (warps 0-3)
   const uint32_t t_row = tmem_d + (static_cast<uint32_t>(warp * 32) << 16);
-  int32_t* red = reinterpret_cast<int32_t*>(exp_base);
   if (warp < 4) {
     if (!mbar_wait(tmem_full, 0, abort_flag)) tile_ok = false;
     if (*abort_flag) tile_ok = false;
     tile_ok = __all_sync(0xffffffffu, tile_ok);
     tc_fence_after();
-    if (SPLIT && z != 0 && tile_ok) {
+  }
+  if constexpr (!SPLIT) {
+    if (warp < 4 && tile_ok) {
+      for (int j0 = 0; j0 < BN; j0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_row + j0, r);
+        tmem_ld_wait();
+        int32_t acc[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) acc[t] = static_cast<int32_t>(r[t]) >> 8;
+        epilogue16<BN, SWAP>(p, ti, tj, row_local, j0, acc);
+      }
+    }
+  } else {
+    // Split K: every CTA of the cluster stages its partial tile (true sums) in its shared memory;
+    // then the tile's (row, 16-column) chunks are dealt out round-robin over the CTAs, and each CTA
+    // sums its chunks over all partials through DSMEM (the loads of one chunk are independent) and
+    // runs the epilogue on them with all of its threads.
+    int32_t* red = reinterpret_cast<int32_t*>(exp_base);
+    if (warp < 4 && tile_ok) {
       for (int j0 = 0; j0 < BN; j0 += 16) {
         uint32_t r[16];
         tmem_ld16(t_row + j0, r);
@@ -432,36 +450,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                              static_cast<int>(r[4 * q + 2]) >> 8, static_cast<int>(r[4 * q + 3]) >> 8);
       }
     }
-  }
-  __syncwarp();
-  if constexpr (SPLIT) cluster_sync();
-  if (warp < 4 && (!SPLIT || z == 0) && tile_ok) {
-    for (int j0 = 0; j0 < BN; j0 += 16) {
-      uint32_t r[16];
-      tmem_ld16(t_row + j0, r);
-      tmem_ld_wait();
+    __syncwarp();
+    cluster_sync();
+    constexpr int kChunksPerRow = BN / 16;
+    const int nsplit = p.splits;
+    for (int item = z + nsplit * static_cast<int>(threadIdx.x); item < 128 * kChunksPerRow;
+         item += nsplit * static_cast<int>(blockDim.x)) {
+      const int row = item / kChunksPerRow, j0 = (item % kChunksPerRow) * 16;
+      const uint32_t local = smem_u32(red + row * C::kRedStride + j0);
       int32_t acc[16];
 #pragma unroll
-      for (int t = 0; t < 16; ++t) acc[t] = static_cast<int32_t>(r[t]) >> 8;
-      if constexpr (SPLIT) {
-        const uint32_t local = smem_u32(red + row_local * C::kRedStride + j0);
-        for (int q = 1; q < p.splits; ++q) {
-          const uint32_t peer = dsmem_map(local, static_cast<uint32_t>(q));
+      for (int t = 0; t < 16; ++t) acc[t] = 0;
+      // up to four partials per batch: all of a batch's remote loads are issued before any sum, so a
+      // batch costs one DSMEM round trip
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const int4 x = dsmem_ld_v4(peer + 16 * v);
-            acc[4 * v] += x.x;
-            acc[4 * v + 1] += x.y;
-            acc[4 * v + 2] += x.z;
-            acc[4 * v + 3] += x.w;
+      for (int q0 = 0; q0 < 8; q0 += 4) {
+        if (q0 < nsplit) {
+          int4 x[4][4];
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            if (q0 + qq < nsplit) {
+              const uint32_t src = dsmem_map(local, static_cast<uint32_t>(q0 + qq));
+#pragma unroll
+              for (int v = 0; v < 4; ++v) x[qq][v] = dsmem_ld_v4(src + 16 * v);
+            } else {
+#pragma unroll
+              for (int v = 0; v < 4; ++v) x[qq][v] = make_int4(0, 0, 0, 0);
+            }
           }
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              acc[4 * v] += x[qq][v].x;
+              acc[4 * v + 1] += x[qq][v].y;
+              acc[4 * v + 2] += x[qq][v].z;
+              acc[4 * v + 3] += x[qq][v].w;
+            }
         }
       }
-      epilogue16<BN, SWAP>(p, ti, tj, row_local, j0, acc);
+      epilogue16<BN, SWAP>(p, ti, tj, row, j0, acc);
     }
+    __syncwarp();
+    cluster_sync();  // no CTA leaves while a peer may still read its partial tile
   }
-  __syncwarp();
-  if constexpr (SPLIT) cluster_sync();
 
   tc_fence_before();
   __syncthreads();
@@ -684,8 +716,16 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
 // CTAs' epilogue warps arrive on the leader's `tmem_empty`.
 //   warps 0-7 epilogue, warp 8 TMEM allocator + MMA issuer (leader) or relay
 //   (peer), warp 9 TMA producer, warps 10-17 expansion (576 threads).
+#ifndef DSCQ_PAIR_EXP_GROUPS
+#define DSCQ_PAIR_EXP_GROUPS 2
+#endif
 struct PairCfg {
   static constexpr int BN = 256;                    // pair tile N (128 B rows per CTA)
+  // The 8 expansion warps form GROUPS groups that expand alternate K blocks, so the load ->
+  // expand -> proxy fence -> arrive latency of one K block overlaps the next one's.
+  static constexpr int GROUPS = DSCQ_PAIR_EXP_GROUPS;
+  static constexpr int kGroupWarps = kExpandWarps / GROUPS;
+  static constexpr int kGroupThreads = kGroupWarps * 32;
   static constexpr int kRows = 256;                 // 128 A rows + 128 B rows per CTA
   static constexpr int kRawStage = kRows * 64;      // 16 KB
   static constexpr int kExpHalf = 128 * 128;        // 16 KB
@@ -694,7 +734,7 @@ struct PairCfg {
   // leader signalling of a stage, the rest of the budget is raw (TMA) stages.
   static constexpr int ES = 4;
   static constexpr int RS = (212 * 1024 - ES * kExpStage - static_cast<int>(sizeof(EpiStage<256>))) / kRawStage;
-  static constexpr int UPT = kRows * 4 / kExpandThreads;
+  static constexpr int UPT = kRows * 4 / kGroupThreads;  // 16-byte chunks per thread and K block
   static constexpr int kTmemCols = 2 * BN;          // two accumulators x 256 columns
   // barriers, TMEM slot and abort flag, then 16-byte signal slots: [ES] copy targets + 1 source
   static constexpr int kSigOff = ((2 * RS + 2 * ES + 5) * 8 + 8 + 15) / 16 * 16;
@@ -737,11 +777,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < RS; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], kExpandWarps);
+      mbar_init(&raw_empty[s], C::kGroupWarps);
     }
     for (int s = 0; s < ES; ++s) {
-      // 8 expansion warps; on the leader the first one also arms 16 bytes for the peer's signal
-      mbar_init(&exp_full[s], kExpandWarps);
+      // the expansion warps of one group; on the leader its first warp also arms 16 bytes for the
+      // peer's signal
+      mbar_init(&exp_full[s], C::kGroupWarps);
       mbar_init(&exp_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -851,11 +892,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
   } else if (warp >= 10) {
     // ------------------------------------------------ int4 -> int8 expansion (both CTAs)
-    const int et = threadIdx.x - 10 * 32;
+    const int grp = (warp - 10) / C::kGroupWarps;                    // group: K blocks g = grp (mod GROUPS)
+    const int et = threadIdx.x - 10 * 32 - grp * C::kGroupThreads;  // thread within the group
+    const bool armer = leader && (warp - 10) % C::kGroupWarps == 0;
     int g = 0;
     bool ok = true;
     for (int tile = pair; ok && tile < ntiles; tile += npairs) {
       for (int kb = 0; kb < kb_n; ++kb, ++g) {
+        if (g % C::GROUPS != grp) continue;
         const int rs = g % RS, es = g % ES;
         if (!mbar_wait(&raw_full[rs], (g / RS) & 1u, abort_flag) ||
             (g >= ES && !mbar_wait_cluster(&exp_empty[es], ((g / ES) & 1u) ^ 1u, abort_flag))) {
@@ -866,12 +910,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         uint8_t* dstA = exp_base + es * C::kExpStage;
         uint4 w[C::UPT];
 #pragma unroll
-        for (int i = 0; i < C::UPT; ++i) w[i] = *reinterpret_cast<const uint4*>(src + (et + i * kExpandThreads) * 16);
+        for (int i = 0; i < C::UPT; ++i)
+          w[i] = *reinterpret_cast<const uint4*>(src + (et + i * C::kGroupThreads) * 16);
 #pragma unroll
         for (int i = 0; i < C::UPT; ++i) {
-          const int u = et + i * kExpandThreads;
+          const int u = et + i * C::kGroupThreads;
           const int row = u >> 2;
-          if (i * kExpandThreads < 128 * 4)
+          if (i * C::kGroupThreads < 128 * 4)
             expand_chunk(w[i], dstA, row, u & 3);
           else
             expand_chunk(w[i], dstA + C::kExpHalf, row - 128, u & 3);
@@ -880,7 +925,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&raw_empty[rs]);
-          if (leader && warp == 10)
+          if (armer)
             mbar_arrive_expect_tx(&exp_full[es], 16);  // + the 16 bytes the peer's relay copies in
           else
             mbar_arrive(&exp_full[es]);

@@ -240,6 +240,36 @@ class QuantLinear(nn.Module):
                               bias=bias, out_dtype=x.dtype)
         return y.reshape(*x.shape[:-1], N)
 
+    # ------------------------------------------------------------------ shared-input projections
+    def quantize_input(self, x2: torch.Tensor) -> "ops.RowQuant":
+        """Rotate+quantize a [M, K] input once for several projections that read it (q/k/v, gate/up
+        of one layer). Their weights must use the same scheme and K; the result feeds
+        forward_quantized of each of them."""
+        if self._prep is None:
+            self.prepare()
+        if "head_rot" in self._prep or not self.symmetric:
+            raise NotImplementedError("quantize_input covers the symmetric scheme without online head rotation")
+        p = self._prep
+        return ops.rowquant(x2, "act_sym", clip=p["aclip"], rotate=self.rotate, KP=p["KP"])
+
+    def forward_quantized(self, q: "ops.RowQuant", M: int, residual: torch.Tensor | None = None,
+                          out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        """This projection on an input already quantised by quantize_input (same K and scheme): the W4A4
+        GEMM with the dequant epilogue, plus an optional [M, N] residual added in the epilogue."""
+        if self._prep is None:
+            self.prepare()
+        p = self._prep
+        if q.KP != p["KP"]:
+            raise ValueError(f"quantised input has KP={q.KP}, this layer expects {p['KP']}")
+        bias = None
+        if p["bias"] is not None:
+            bias = p["bias_cache"].get(out_dtype)
+            if bias is None:
+                bias = p["bias"].to(out_dtype).contiguous()
+                p["bias_cache"][out_dtype] = bias
+        return ops.w4a4_gemm(q.packed, p["packed"], q.scales, p["sw"], M=M, N=p["N"], bias=bias, residual=residual,
+                             out_dtype=out_dtype)
+
     def extra_repr(self) -> str:
         return (f"in={self.base.in_features}, out={self.base.out_features}, symmetric={self.symmetric}, "
                 f"rotation={self.rotate}, enabled={self.enabled}")

@@ -82,6 +82,7 @@ class ColumnParallelQuantLinear:
         self.rotate = rotate
         self.mode = mode
         self.copy_out = copy_out
+        self.timeline = None  # set to a list to record (phase, CUDA event) pairs at phase boundaries
         self.device = weight_shard.device
         q = ops.rowquant(weight_shard.contiguous(), "weight_sym", rotate=rotate, KP=self.KP)
         self.w_packed, self.sw = q.packed, q.scales
@@ -104,6 +105,12 @@ class ColumnParallelQuantLinear:
             self.s_peer = [self.s_hdl.get_buffer(r, (max_tokens,), torch.float32) for r in range(self.world)]
             self.h_rot = ops.rotation_factor(self.K, self.device) if rotate else (1, None)
 
+    def _mark(self, phase: str) -> None:
+        if self.timeline is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream(self.device))
+            self.timeline.append((phase, ev))
+
     def _local_block(self, q, M: int) -> torch.Tensor:
         return ops.w4a4_gemm(q.packed, self.w_packed, q.scales, self.sw, M=M, N=self.hi - self.lo, bias=self.bias)
 
@@ -111,12 +118,18 @@ class ColumnParallelQuantLinear:
         if not x.is_cuda or x.dtype != torch.bfloat16:
             raise RuntimeError("ColumnParallelQuantLinear expects a bf16 CUDA input")
         M = x.shape[0]
+        self._mark("start")
         if self.mode == "nccl":
             q = ops.rowquant(x.contiguous(), "act_sym", rotate=self.rotate, KP=self.KP)
+            self._mark("quantize")
             block = self._local_block(q, M)
+            self._mark("gemm")
             gathered = torch.empty((self.world, M, self.hi - self.lo), dtype=block.dtype, device=block.device)
             dist.all_gather_into_tensor(gathered, block, group=self.group)
-            return assemble(gathered)
+            self._mark("all_gather")
+            y = assemble(gathered)
+            self._mark("assemble")
+            return y
         if M > self.max_tokens:
             raise RuntimeError(f"M={M} exceeds max_tokens={self.max_tokens} of the symmetric output buffer")
         q = self._quantize_rows_sharded(x.contiguous(), M)
@@ -125,7 +138,9 @@ class ColumnParallelQuantLinear:
                                          self.KP, _lib.BF16, self.peer_ptrs, self.world, self.N, self.lo, 0,
                                          ops._stream(self.device))
         _lib.check(rc, "dscq_matmul_cols")
+        self._mark("gemm_peer_stores")
         self.hdl.barrier(channel=2)
+        self._mark("barrier_out")
         return self.out[:M].clone() if self.copy_out else self.out[:M]
 
     def _quantize_rows_sharded(self, x: torch.Tensor, M: int):
@@ -133,6 +148,7 @@ class ColumnParallelQuantLinear:
         buffers, then copies the other ranks' packed rows and scales over NVLink (peer reads), so every
         rank holds the full packed activations after 1/p of the quantisation work."""
         self.hdl.barrier(channel=0)  # every rank is done reading last call's buffers
+        self._mark("barrier_in")
         lo, hi = row_bounds(M, self.world, self.rank)
         if hi > lo:
             a, h = self.h_rot
@@ -142,7 +158,9 @@ class ColumnParallelQuantLinear:
                                           ops._ptr(self.a_sym[lo:hi]), self.KP // 2, ops._ptr(self.s_sym[lo:hi]),
                                           None, None, None, 0, ops._stream(self.device))
             _lib.check(rc, "rowquant")
+        self._mark("quantize_rows")
         self.hdl.barrier(channel=1)  # all row blocks written
+        self._mark("barrier_rows")
         for r in range(self.world):
             if r == self.rank:
                 continue
@@ -150,4 +168,5 @@ class ColumnParallelQuantLinear:
             if rhi > rlo:
                 self.a_sym[rlo:rhi].copy_(self.a_peer[r][rlo:rhi], non_blocking=True)
                 self.s_sym[rlo:rhi].copy_(self.s_peer[r][rlo:rhi], non_blocking=True)
+        self._mark("gather_rows")
         return self.a_sym, self.s_sym

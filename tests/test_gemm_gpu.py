@@ -59,7 +59,10 @@ def _run(oracle, dev, M, N, KP, variant="auto", asym=False, bias=False, residual
 
 
 SHAPES = [(1, 128, 128), (7, 96, 64), (9, 200, 192), (16, 4096, 4096), (33, 130, 320), (64, 256, 256),
-          (65, 300, 320), (128, 256, 1024), (200, 520, 448), (256, 512, 1024), (512, 1024, 512), (300, 1000, 2048)]
+          (65, 300, 320), (128, 256, 1024), (200, 520, 448), (256, 512, 1024), (512, 1024, 512), (300, 1000, 2048),
+          # split K over clusters of 2..8 CTAs with the reduction spread over the cluster (128- and 256-wide tiles)
+          (128, 4096, 4096), (128, 1024, 4096), (48, 4096, 2048), (128, 11008, 4096), (300, 4864, 2048),
+          (128, 14336, 1024), (512, 4096, 4096), (100, 9728, 1088)]
 
 
 @pytest.mark.parametrize("M,N,KP", SHAPES)

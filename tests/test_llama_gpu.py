@@ -1,0 +1,37 @@
+"""The Llama-2 prefill harness (dscquant_b200/llama.py) on a small configuration: shared-input projections
+(one rotate+quantize feeding q/k/v or gate/up) give the same bits as each QuantLinear's own forward, the
+residual added in the GEMM epilogue equals a separate add, and a prefill is finite and deterministic."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_shared_input_projection_matches_forward(cuda_device):
+    from dscquant_b200.llama import random_quant_linear
+
+    g = torch.Generator(device=cuda_device).manual_seed(0)
+    a = random_quant_linear(384, 1024, g, cuda_device)
+    b = random_quant_linear(512, 1024, g, cuda_device)
+    x = torch.randn(70, 1024, generator=g, device=cuda_device).to(torch.bfloat16)
+    q = a.quantize_input(x)
+    assert torch.equal(a.forward_quantized(q, 70), a(x))
+    assert torch.equal(b.forward_quantized(q, 70), b(x))
+    r = torch.randn(70, 512, generator=g, device=cuda_device).to(torch.bfloat16)
+    fused = b.forward_quantized(q, 70, residual=r)
+    f32 = b.forward_quantized(q, 70, out_dtype=torch.float32)  # the epilogue value before rounding
+    assert torch.equal(fused, (f32 + r.float()).to(torch.bfloat16))  # one rounding of the fp32 sum
+
+
+def test_small_llama_prefill(cuda_device):
+    from dscquant_b200.llama import LlamaConfig, LlamaW4A4
+
+    cfg = LlamaConfig(vocab=512, hidden=1024, heads=8, kv_heads=4, intermediate=2048, layers=2)
+    model = LlamaW4A4(cfg, cuda_device, seed=1)
+    ids = torch.randint(0, cfg.vocab, (96,), device=cuda_device, generator=torch.Generator(device=cuda_device).manual_seed(2))
+    y1 = model(ids)
+    y2 = model(ids)
+    assert y1.shape == (96, cfg.vocab) and y1.dtype == torch.bfloat16
+    assert bool(torch.isfinite(y1.float()).all())
+    assert torch.equal(y1, y2)
+    assert model.linear_ops(96) > 0
