@@ -19,6 +19,7 @@
 #include "rowquant.cuh"
 #include "wht_quant.cuh"
 #include "kron_quant.cuh"
+#include "kron_long_quant.cuh"
 #include "gemv_w4a4.cuh"
 #include "gemm_a8.cuh"
 #include "gemm_pair_tm.cuh"
@@ -690,6 +691,21 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   if (kron) {
     cudaError_t e = ap <= 176 ? launch_kron<176>(p, p.rot_a, s_log, cst) : launch_kron<224>(p, p.rot_a, s_log, cst);
     if (e != cudaSuccess) return cuda_fail(e, "launch kron_quant");
+    return DSCQ_OK;
+  }
+
+  // long rows K = a * 1024 with a dense factor a <= 32 (K = 28672: H_28 (x) H_1024)
+  const bool klong = rotate && p.rot_a > 1 && p.rot_a <= 32 && log2b == 10 &&
+                     (mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM) && x_dtype == DSCQ_BF16 && KP == K &&
+                     aligned(x, 16) && ld_x % 8 == 0;
+  if (klong) {
+    using KC = dscq::KronLongCfg;
+    cudaError_t e = cudaFuncSetAttribute(dscq::kron_long_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, KC::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(kron_long_quant)");
+    const int grid = static_cast<int>(std::min<int64_t>(rows_out, num_sms()));
+    dscq::kron_long_quant<<<grid, KC::THREADS, KC::SMEM, cst>>>(p, p.rot_a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch kron_long_quant");
     return DSCQ_OK;
   }
 

@@ -206,3 +206,28 @@ def test_ste_round_matches_reference(cuda_device):
     np.testing.assert_array_equal(x.grad.cpu().numpy(), d["ste_grad"])
     with pytest.raises(RuntimeError):
         dq.ste_round(torch.zeros(3))  # CUDA tensors only
+
+
+@pytest.mark.parametrize("K", [28672, 20480, 12288])
+@pytest.mark.parametrize("mode", ["act_sym", "weight_sym"])
+def test_rowquant_long_rows_kron(oracle, cuda_device, K, mode):
+    """K = a * 1024 with a dense factor a <= 32 on the long-row kernel (H_a on mma.sync, 1024-point WHT,
+    shared-memory exchange): codes within one step of the oracle only at rounding ties, packed bytes equal
+    to the packing of the codes, code sums exact, padding rows zero, scales to 2e-6."""
+    from dscquant_b200 import ops
+
+    M, rows_out = 37, 40
+    bits = synthetic.activations_bf16(M, K, seed=K + 5) if mode == "act_sym" else synthetic.weights_bf16(M, K, seed=K)
+    r = ops.rowquant(_tbf(bits, cuda_device), mode, rotate=True, KP=K, rows_out=rows_out, codes=True, row_sums=True,
+                     variant="legacy")
+    y = oracle.rotate_c(_f32(bits))
+    ref = oracle.quant_rows(y, MODES[mode], 1.0, KP=K)
+    np.testing.assert_allclose(r.scales.cpu().numpy()[:M], ref["scales"], rtol=2e-6)
+    c = r.codes.cpu().numpy().astype(np.int32)
+    diff = c[:M] != ref["codes"].astype(np.int32)
+    assert np.all(np.abs(c[:M] - ref["codes"])[diff] == 1) and diff.mean() < 1e-3
+    q = y[diff] / ref["scales"][np.nonzero(diff)[0]]
+    assert np.all(_near_tie(q))
+    np.testing.assert_array_equal(r.row_sums.cpu().numpy(), c.sum(1))
+    np.testing.assert_array_equal(r.packed.cpu().numpy(), oracle.pack_int4(c.astype(np.int8)))
+    assert not c[M:].any() and np.all(r.scales.cpu().numpy()[M:] <= 1e-7)
