@@ -615,8 +615,8 @@ def prefill_record(dev, seq: int = 2048, reps: int = 5) -> dict:
            "tokens_per_s": seq / (ms * 1e-3), "ms_per_prefill": ms, "reps": reps,
            "w4a4_linear_tops": model.linear_ops(seq) / (ms * 1e-3) / 1e12, "logits_finite": ok,
            "note": "all 224 projections + LM head W4A4 (rotate+quantize shared by q/k/v and by gate/up, residuals "
-                   "added in the GEMM epilogue); attention bf16 torch SDPA; RMSNorm / RoPE / SiLU torch ops; "
-                   "random-init weights, uniform random token ids"}
+                   "added in the GEMM epilogue); RMSNorm / RoPE / SiLU-gate as single-pass bf16 kernels of this "
+                   "package; causal attention bf16 torch SDPA; random-init weights, uniform random token ids"}
     del model
     torch.cuda.empty_cache()
     return rec

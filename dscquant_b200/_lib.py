@@ -45,6 +45,9 @@ SIGNATURES = {
                                 ctypes.POINTER(ctypes.c_void_p), _i32, _i64, _i64, _i32, _vp]),
     "dscq_rowquant_tc_noalloc": (_i32, [_vp, _i32, _i64, _i64, _i64, _i32, _i32, _vp, _i32, _f32, _i64, _i64, _vp,
                                         _i64, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "dscq_rmsnorm": (_i32, [_vp, _vp, _i64, _i64, _f32, _vp, _vp]),
+    "dscq_rope": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp]),
+    "dscq_silu_mul": (_i32, [_vp, _vp, _i64, _vp, _vp]),
     "dscq_pack_int4": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "dscq_unpack_int4": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp]),
 }

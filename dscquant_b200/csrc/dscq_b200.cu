@@ -25,6 +25,7 @@
 #include "gemm_pair_tm.cuh"
 #include "headrot_quant.cuh"
 #include "rotq_tc.cuh"
+#include "llama_ops.cuh"
 
 namespace {
 
@@ -942,6 +943,50 @@ int dscq_matmul_a8_variant(const int8_t* a, int64_t ld_a, const uint8_t* b, cons
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (pair) return launch_gemm_pair_a8(tmA, tmQ, gp, s);
   return BN == 256 ? launch_gemm_a8<256>(tmA, tmQ, gp, s) : launch_gemm_a8<128>(tmA, tmQ, gp, s);
+}
+
+int dscq_rmsnorm(const void* x, const void* w, int64_t rows, int64_t H, float eps, void* y, void* stream) {
+  DSCQ_REQUIRE(x && w && y, "x, w and y must not be null");
+  DSCQ_REQUIRE(rows >= 1 && rows < (int64_t(1) << 31) && H >= 8 && H % 8 == 0 && H <= (1 << 20),
+               "rmsnorm needs rows >= 1 and H a positive multiple of 8");
+  DSCQ_REQUIRE(aligned(x, 16) && aligned(w, 16) && aligned(y, 16), "rmsnorm buffers must be 16-byte aligned");
+  int st = check_device(nullptr);
+  if (st) return st;
+  dscq::rmsnorm_kernel<<<static_cast<unsigned>(rows), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y),
+      static_cast<int>(H), eps);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch rmsnorm");
+  return DSCQ_OK;
+}
+
+int dscq_rope(void* q, void* k, const void* cos_t, const void* sin_t, int64_t S, int Hq, int Hk, int D, void* stream) {
+  DSCQ_REQUIRE(q && k && cos_t && sin_t, "q, k, cos and sin must not be null");
+  DSCQ_REQUIRE(S >= 1 && Hq >= 1 && Hk >= 1 && D >= 2 && D % 2 == 0 && D <= 1024, "invalid rope shape");
+  int st = check_device(nullptr);
+  if (st) return st;
+  const int64_t total = S * (Hq + Hk) * (D / 2);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, int64_t(num_sms()) * 16));
+  dscq::rope_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(cos_t),
+      static_cast<const __nv_bfloat16*>(sin_t), static_cast<int>(S), Hq, Hk, D);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch rope");
+  return DSCQ_OK;
+}
+
+int dscq_silu_mul(const void* g, const void* u, int64_t n, void* y, void* stream) {
+  DSCQ_REQUIRE(g && u && y, "g, u and y must not be null");
+  DSCQ_REQUIRE(n >= 8 && n % 8 == 0, "silu_mul needs n a positive multiple of 8");
+  DSCQ_REQUIRE(aligned(g, 16) && aligned(u, 16) && aligned(y, 16), "silu_mul buffers must be 16-byte aligned");
+  int st = check_device(nullptr);
+  if (st) return st;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n / 8 + 255) / 256, int64_t(num_sms()) * 16));
+  dscq::silu_mul_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(g), static_cast<const __nv_bfloat16*>(u), static_cast<__nv_bfloat16*>(y), n);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch silu_mul");
+  return DSCQ_OK;
 }
 
 int dscq_pack_int4(const int8_t* codes, int64_t rows, int64_t K, int64_t ld_codes, uint8_t* packed,

@@ -212,9 +212,62 @@ __device__ __forceinline__ void epilogue_stage(const GemmParams& p, int tj, int 
 
 // SH: the accumulator holds 2^SH * sum(a * b) (8: both operands expanded as 16 * code; 4: int8
 // activation codes times expanded weights).
+// Multi-buffer output (the column-parallel all-gather writes every tile into every GPU's buffer):
+// the warp stages 32 rows x 32 columns of bf16 (2 KB, `stg`) and then writes whole 64-byte row
+// segments, four lanes per row, instead of one 32-byte piece per lane and row; peer writes over
+// NVLink move in larger, fully used transfers. bf16 output, N a multiple of 32, no raw / residual.
+template <int BN, int SH>
+__device__ __forceinline__ void epilogue_tile_staged(const GemmParams& p, int ti, int tj, uint32_t t_row, int q, int h,
+                                                     int lane, const EpiStage<BN>* st, int par, float sxm, int32_t zc,
+                                                     uint8_t* stg) {
+  const bool asym = p.zx != nullptr, has_bias = p.bias != nullptr;
+#pragma unroll 1
+  for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 32) {
+    uint32_t r0[16], r1[16];
+    tmem_ld16(t_row + static_cast<uint32_t>(c0), r0);
+    tmem_ld16(t_row + static_cast<uint32_t>(c0 + 16), r1);
+    tmem_ld_wait();
+    const int n0 = tj * BN + c0;
+    if (n0 >= p.N) continue;  // N is a multiple of 32: the chunk is wholly inside or outside
+    uint32_t w[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      float f2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int c = 2 * t + e;
+        int32_t a = static_cast<int32_t>(c < 16 ? r0[c] : r1[c - 16]) >> SH;
+        if (asym) a += zc * st->wsum[par][c0 + c];
+        float f = epi_scale(a, sxm, st->sw[par][c0 + c]);
+        if (has_bias) f = __fadd_rn(f, st->bias[par][c0 + c]);
+        f2[e] = f;
+      }
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(f2[0], f2[1]);
+      w[t] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)  // this lane's row: four 16-byte chunks, XOR-swizzled by row
+      *reinterpret_cast<uint4*>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+          make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // rows 8k .. 8k+7: four lanes per 64-byte row segment
+      const int rr = 8 * k + (lane >> 2), ch = lane & 3;
+      const int m = ti * 128 + q * 32 + rr;
+      if (m < p.M) {
+        const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 64 + ((ch ^ ((rr >> 1) & 3)) << 4));
+        const int64_t o = static_cast<int64_t>(m) * p.ld_out + p.col_off + n0 + ch * 8;
+        for (int b = 0; b < p.n_outs; ++b)
+          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.outs[b]) + o) = v;
+      }
+    }
+    __syncwarp();
+  }
+}
+
 template <int BN, int SH = 8>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int tj, uint32_t tmem_acc, int ew, int lane,
-                                              const EpiStage<BN>* st, int par) {
+                                              const EpiStage<BN>* st, int par, uint8_t* stg = nullptr) {
   const int q = ew & 3, h = ew >> 2;
   const int row_local = q * 32 + lane;
   const int m = ti * 128 + row_local;
@@ -223,6 +276,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int ti, int t
   const bool asym = p.zx != nullptr, has_bias = p.bias != nullptr, has_res = p.residual != nullptr;
   const float sxm = live ? p.sx[m] : 0.f;
   const int32_t zc = (asym && live) ? 8 - p.zx[m] : 0;
+  if (stg != nullptr && p.n_outs > 1 && p.vec_out && p.out_dtype == kOutBF16 && p.raw == nullptr && !has_res &&
+      p.N % 32 == 0) {
+    epilogue_tile_staged<BN, SH>(p, ti, tj, t_row, q, h, lane, st, par, sxm, zc, stg);
+    return;
+  }
 #pragma unroll 1
   for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 16) {
     uint32_t r[16];
@@ -740,7 +798,8 @@ struct PairCfg {
   static constexpr int kSigOff = ((2 * RS + 2 * ES + 5) * 8 + 8 + 15) / 16 * 16;
   static constexpr int kBarBytes = kSigOff + (ES + 1) * 16;
   static constexpr int kEpiBytes = static_cast<int>(sizeof(EpiStage<BN>));
-  static constexpr int kSmemBytes = 1024 + ES * kExpStage + RS * kRawStage + kBarBytes + kEpiBytes;
+  static constexpr int kStgBytes = kEpiWarps * 2048;  // staged multi-buffer epilogue, 2 KB per warp
+  static constexpr int kSmemBytes = 1024 + ES * kExpStage + RS * kRawStage + kBarBytes + kEpiBytes + kStgBytes;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -765,6 +824,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint8_t* sig = reinterpret_cast<uint8_t*>(bars) + C::kSigOff;  // [ES] copy targets, then the source
   EpiStage<BN>* est = reinterpret_cast<EpiStage<BN>*>(reinterpret_cast<uint8_t*>(bars) + C::kBarBytes);
+  uint8_t* stg_base = reinterpret_cast<uint8_t*>(bars) + C::kBarBytes + C::kEpiBytes;  // 16-byte aligned
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -944,7 +1004,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       ok = named_bar_and(1, kEpiThreads, ok && !*abort_flag);
       if (!ok) break;
       tc_fence_after();
-      epilogue_tile<BN>(p, ti, tj, tmem_base + static_cast<uint32_t>(acc_i * BN), warp, lane, est, t & 1);
+      epilogue_tile<BN>(p, ti, tj, tmem_base + static_cast<uint32_t>(acc_i * BN), warp, lane, est, t & 1,
+                        stg_base + warp * 2048);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tmem_empty_ldr + static_cast<uint32_t>(acc_i * 8));

@@ -18,8 +18,10 @@ run without the transformers model code or a checkpoint:
     logits = Wlm RMSNorm(h)
 
 All seven projections of every layer and the LM head are W4A4 (symmetric per-token activations,
-online Hadamard rotation, symmetric per-channel int4 weights). Attention, RMSNorm, RoPE and the
-SiLU gate stay in bf16/fp32 torch ops: they are not part of the quantized-linear path.
+online Hadamard rotation, symmetric per-channel int4 weights). RMSNorm, RoPE and the SiLU gate are
+single-pass bf16 kernels of this package (ops.rmsnorm / rope_ / silu_mul, the same rounding steps as
+the torch expressions rms_norm / apply_rope below, which the tests compare them with); causal
+attention is torch's scaled_dot_product_attention in bf16.
 """
 from __future__ import annotations
 
@@ -28,6 +30,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
+from . import ops
 from .linear import QuantConfig, QuantLinear
 
 
@@ -95,21 +98,21 @@ class DecoderLayer:
     def __call__(self, h: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
         cfg = self.cfg
         S = h.shape[0]
-        x = rms_norm(h, self.norm1, cfg.eps)
+        x = ops.rmsnorm(h, self.norm1, cfg.eps)
         qx = self.q.quantize_input(x)
         q = self.q.forward_quantized(qx, S).view(S, cfg.heads, cfg.head_dim)
         k = self.k.forward_quantized(qx, S).view(S, cfg.kv_heads, cfg.head_dim)
         v = self.v.forward_quantized(qx, S).view(S, cfg.kv_heads, cfg.head_dim)
-        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        ops.rope_(q, k, cos, sin)
         a = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None], v.transpose(0, 1)[None],
                                            is_causal=True, enable_gqa=cfg.kv_heads != cfg.heads)
         a = a[0].transpose(0, 1).reshape(S, cfg.hidden)
         h = self.o.forward_quantized(self.o.quantize_input(a), S, residual=h)
-        x = rms_norm(h, self.norm2, cfg.eps)
+        x = ops.rmsnorm(h, self.norm2, cfg.eps)
         gx = self.gate.quantize_input(x)
         g = self.gate.forward_quantized(gx, S)
         u = self.up.forward_quantized(gx, S)
-        m = F.silu(g) * u
+        m = ops.silu_mul(g, u)
         return self.down.forward_quantized(self.down.quantize_input(m), S, residual=h)
 
 
@@ -139,7 +142,7 @@ class LlamaW4A4:
         h = self.embed[ids]
         for layer in self.layers:
             h = layer(h, cos, sin)
-        x = rms_norm(h, self.norm, self.cfg.eps)
+        x = ops.rmsnorm(h, self.norm, self.cfg.eps)
         return self.lm_head.forward_quantized(self.lm_head.quantize_input(x), S)
 
     def linear_ops(self, S: int) -> float:

@@ -354,3 +354,44 @@ def unpack_int4_cuda(packed: torch.Tensor, width: int) -> torch.Tensor:
             rc = _lib.load().dscq_unpack_int4(_ptr(p), rows, p.size(1), w, _ptr(codes), w, _stream(p.device))
             _lib.check(rc, "unpack_int4")
     return codes
+
+
+# ------------------------------------------------------------------ prefill element-wise operators
+def _bf16_cuda(t: torch.Tensor, name: str) -> None:
+    if not (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous()):
+        raise RuntimeError(f"{name} must be a contiguous bf16 CUDA tensor")
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """bf16(bf16(x * rsqrt(mean(x^2, -1) + eps)) * w) over the last dimension, one kernel."""
+    _bf16_cuda(x, "x")
+    _bf16_cuda(w, "w")
+    H = x.shape[-1]
+    if w.numel() != H:
+        raise RuntimeError("w must have the last dimension of x")
+    y = torch.empty_like(x)
+    _lib.check(_lib.load().dscq_rmsnorm(_ptr(x), _ptr(w), x.numel() // H, H, float(eps), _ptr(y), _stream(x.device)),
+               "rmsnorm")
+    return y
+
+
+def rope_(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> None:
+    """Rotary embeddings (rotate-half form) in place on q [S, Hq, D] and k [S, Hk, D]; cos / sin [S, D]."""
+    for name, t in (("q", q), ("k", k), ("cos", cos), ("sin", sin)):
+        _bf16_cuda(t, name)
+    S, Hq, D = q.shape
+    if k.shape[0] != S or k.shape[2] != D or cos.shape != (S, D) or sin.shape != (S, D):
+        raise RuntimeError("rope shapes: q [S, Hq, D], k [S, Hk, D], cos / sin [S, D]")
+    _lib.check(_lib.load().dscq_rope(_ptr(q), _ptr(k), _ptr(cos), _ptr(sin), S, Hq, k.shape[1], D, _stream(q.device)),
+               "rope")
+
+
+def silu_mul(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """bf16(bf16(silu(g)) * u), one kernel."""
+    _bf16_cuda(g, "g")
+    _bf16_cuda(u, "u")
+    if g.shape != u.shape:
+        raise RuntimeError("g and u must have the same shape")
+    y = torch.empty_like(g)
+    _lib.check(_lib.load().dscq_silu_mul(_ptr(g), _ptr(u), g.numel(), _ptr(y), _stream(g.device)), "silu_mul")
+    return y

@@ -204,6 +204,19 @@ int dscq_rowquant_tc_noalloc(const void* x, int x_dtype, int64_t M, int64_t K, i
                              int64_t ld_packed, float* scales, int32_t* zeros, int32_t* row_sums, int8_t* codes,
                              int64_t ld_codes, void* stream);
 
+/*
+ * Element-wise operators of the Llama prefill workload around the W4A4 linears (no counterpart in the
+ * reference, which runs a Hugging Face model around its QuantLinear). bf16 tensors, fp32 arithmetic,
+ * rounded to bf16 at the same steps as the torch expressions in the comments.
+ *   dscq_rmsnorm:  y[r] = bf16(bf16(x[r] * rsqrt(mean(x[r]^2) + eps)) * w), x, y [rows, H], w [H]
+ *   dscq_rope:     in place, q [S, Hq, D] and k [S, Hk, D]: x = bf16(bf16(x * cos) + bf16(rot(x) * sin)),
+ *                  rot(x) = [-x[D/2:], x[:D/2]], cos / sin [S, D]
+ *   dscq_silu_mul: y = bf16(bf16(silu(g)) * u), n elements
+ */
+int dscq_rmsnorm(const void* x, const void* w, int64_t rows, int64_t H, float eps, void* y, void* stream);
+int dscq_rope(void* q, void* k, const void* cos_t, const void* sin_t, int64_t S, int Hq, int Hk, int D, void* stream);
+int dscq_silu_mul(const void* g, const void* u, int64_t n, void* y, void* stream);
+
 /* pack_int4, core/quantization.py:31-40. codes [rows, K] int8 (row stride
  * ld_codes) -> packed [rows, ceil(K/2)] (row stride ld_packed). Codes outside
  * [-8, 7] are counted into *bad_count (device int, caller-zeroed). */

@@ -35,3 +35,34 @@ def test_small_llama_prefill(cuda_device):
     assert bool(torch.isfinite(y1.float()).all())
     assert torch.equal(y1, y2)
     assert model.linear_ops(96) > 0
+
+
+def test_prefill_elementwise_ops_match_torch(cuda_device):
+    """ops.rmsnorm / rope_ / silu_mul against the torch expressions of the harness: RoPE bit-exact (same
+    rounding steps); RMSNorm and the SiLU gate within one bf16 step (the row sum of squares, rsqrt and exp
+    may round differently from torch's kernels)."""
+    import torch.nn.functional as F
+
+    from dscquant_b200 import ops
+    from dscquant_b200.llama import apply_rope, rms_norm, rope_tables
+
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    S, H, D = 300, 12, 128
+    x = (torch.randn(S, H * D, generator=g, device=cuda_device) * 3).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H * D, generator=g, device=cuda_device)).to(torch.bfloat16)
+    ref = rms_norm(x, w, 1e-5)
+    out = ops.rmsnorm(x, w, 1e-5)
+    ulp = (ref.float().abs() * 2 ** -7).clamp_min(1e-30)
+    assert bool(((out.float() - ref.float()).abs() <= ulp).all())
+    cos, sin = rope_tables(S, D, 10000.0, cuda_device)
+    q = torch.randn(S, H, D, generator=g, device=cuda_device).to(torch.bfloat16)
+    k = torch.randn(S, 4, D, generator=g, device=cuda_device).to(torch.bfloat16)
+    rq, rk = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+    ops.rope_(q, k, cos, sin)
+    assert torch.equal(q, rq) and torch.equal(k, rk)
+    a = (torch.randn(S, 1000, generator=g, device=cuda_device) * 4).to(torch.bfloat16)
+    b = torch.randn(S, 1000, generator=g, device=cuda_device).to(torch.bfloat16)
+    ref = F.silu(a) * b
+    out = ops.silu_mul(a, b)
+    ulp = (ref.float().abs() * 2 ** -7).clamp_min(1e-30)
+    assert bool(((out.float() - ref.float()).abs() <= ulp).all())

@@ -4,7 +4,8 @@ every shard into every rank's output buffer. Local buffers stand in for the peer
 residual read at the same [m, col_off + n] positions), and every other column must stay untouched.
 Covers every GEMM kernel (decode, tcgen05 swap / split-K, 1-CTA persistent, direct-load, CTA pair,
 TMEM-activation pair), the 16-byte vector stores (col_off a multiple of 8) and the scalar fallback
-(col_off = 8k + 4), with and without bias and residual."""
+(col_off = 8k + 4), with and without bias and residual; with several bf16 buffers and 16-byte aligned
+columns the CTA-pair kernel stages each warp's rows in shared memory and stores whole row segments."""
 import ctypes
 
 import numpy as np
@@ -22,7 +23,7 @@ VARIANTS = {"auto": 0, "small_m": 1, "large_m": 2, "large_m_direct": 3, "large_m
 
 @pytest.mark.parametrize("M,variant", CASES)
 @pytest.mark.parametrize("where", ["zero", "second_block", "unaligned"])
-@pytest.mark.parametrize("extras", [False, True])
+@pytest.mark.parametrize("extras", ["none", "bias", "bias_residual"])
 def test_matmul_cols_matches_matmul(cuda_device, M, variant, where, extras):
     from dscquant_b200 import _lib, ops
 
@@ -35,9 +36,10 @@ def test_matmul_cols_matches_matmul(cuda_device, M, variant, where, extras):
     b = torch.randint(0, 256, (N, KP // 2), generator=g, device=cuda_device, dtype=torch.uint8)
     sx = torch.rand(M, generator=g, device=cuda_device) * 0.01 + 1e-3
     sw = torch.rand(N, generator=g, device=cuda_device) * 0.01 + 1e-3
-    bias = torch.randn(N, generator=g, device=cuda_device).to(torch.bfloat16) if extras else None
-    res_full = torch.randn(M, ld_out, generator=g, device=cuda_device).to(torch.bfloat16) if extras else None
-    res_block = res_full[:, col_off:col_off + N].contiguous() if extras else None
+    bias = torch.randn(N, generator=g, device=cuda_device).to(torch.bfloat16) if extras != "none" else None
+    res_full = (torch.randn(M, ld_out, generator=g, device=cuda_device).to(torch.bfloat16)
+                if extras == "bias_residual" else None)
+    res_block = res_full[:, col_off:col_off + N].contiguous() if res_full is not None else None
     ref = ops.w4a4_gemm(a, b, sx, sw, bias=bias, residual=res_block, variant=variant)
 
     sentinel = torch.tensor(-12345.0, dtype=torch.bfloat16)
