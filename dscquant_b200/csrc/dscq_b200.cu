@@ -779,12 +779,15 @@ static int matmul_impl(const uint8_t* a, const uint8_t* b, const float* sx, cons
   } else {
     ti = (M + 127) / 128;
     const int64_t t256 = ti * ((N + 255) / 256), t128 = ti * ((N + 127) / 128);
-    auto eff = [&](int64_t t) { return static_cast<double>(t) / (((t + nsm - 1) / nsm) * nsm); };
     if (t128 * 2 <= nsm) {
       BN = 128;  // too few tiles: split K across a cluster
       while (splits < 8 && t128 * splits * 2 <= nsm && kblocks >= splits * 2 * 2) splits *= 2;
     } else {
-      BN = (t256 >= nsm / 2 && eff(t256) + 0.1 >= eff(t128)) ? 256 : 128;
+      // 256-wide tiles (the CTA-pair kernel) whenever every pair gets at least one: a pair tile runs
+      // about 1.9x the int ops per SM-second of a 128-wide 1-CTA tile, which outweighs the better
+      // wave quantisation of the smaller tiles (M = N = 4096, K = 8192 on 128-wide tiles: 0.20 ms,
+      // as long as N = 8192 on pair tiles)
+      BN = t256 >= nsm / 2 ? 256 : 128;
     }
     if (variant == DSCQ_GEMM_LARGE_M_PAIR_TMEM) {  // 256 x 192 pair tiles, activations in TMEM
       BN = 192;

@@ -14,8 +14,8 @@
 //     consumed by tcgen05.mma kind::f16 without any rearrangement;
 //   * H'^T (A operand, K-major, 128 rows per M tile, 128-byte swizzle) is a
 //     constant of K: rotq_build_operand writes its shared-memory image to global
-//     memory once per device and K, and every CTA copies it in with one bulk
-//     copy per 16 KB atom while the first token loads are in flight. For
+//     memory once per device and K, and every CTA copies it in (one bulk copy
+//     per 16 KB atom, hot in L2) ahead of its first token boxes. For
 //     a' <= 64 (a' = 32, 64) P = 128 / a' tokens share one MMA through a
 //     block-diagonal A (k = token*a' + i), so all 128 TMEM lanes carry data;
 //     a' in (128, 256] uses two M tiles;
@@ -251,7 +251,18 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ap = rp.ap, ap16 = rp.ap16, P = rp.P, ns = rp.ns, tw = rp.tw;
 
-  if (threadIdx.x == 0) {
+  const int groups = rp.groups;
+  const int my_blocks = groups > static_cast<int>(blockIdx.x)
+                            ? (groups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                                  static_cast<int>(gridDim.x)
+                            : 0;
+  // The TMA thread initialises every barrier and starts its copies before the CTA barrier, so the
+  // DRAM reads overlap the TMEM allocation and the other warps' start-up: first the A operand (a
+  // constant of K, prebuilt in global memory and hot in L2, needed before the first MMA), then one
+  // ring's worth of token boxes (no stage can be busy yet).
+  int n_pre = 0;
+  if (warp == rp.tma_warp && lane == 0) {
+    tma_prefetch_desc(&tmX);
     for (int s = 0; s < ns; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -264,8 +275,15 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
     mbar_init(aready, 1);
     *abort_flag = 0;
     fence_mbar_init();
+    mbar_arrive_expect_tx(aready, rp.a_bytes);
+    for (uint32_t off = 0; off < rp.a_bytes; off += 16384u) bulk_load_g2s(a_base + off, rp.a_op + off, 16384u, aready);
+    n_pre = min(ns, my_blocks);
+    for (int n = 0; n < n_pre; ++n) {
+      const int g = static_cast<int>(blockIdx.x) + n * static_cast<int>(gridDim.x);
+      mbar_arrive_expect_tx(&full[n], rp.stage_bytes);
+      tma_load_3d(b_base + n * rp.stage_bytes, &tmX, &full[n], 0, 0, g * P);
+    }
   }
-  if (warp == rp.tma_warp && lane == 0) tma_prefetch_desc(&tmX);
   if (warp == rp.mma_warp) {
     tmem_alloc(tmem_slot, kRqTmemCols);
     tmem_relinquish();
@@ -274,40 +292,22 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int groups = rp.groups;
   const int team = warp / rp.team_stride, idx = warp % rp.team_stride;
 
   if (warp == rp.tma_warp) {
-    // ------------------------------------------------ TMA producer
+    // ------------------------------------------------ TMA producer: the rest of this CTA's token blocks
     if (lane == 0) {
-      // The A operand (a constant of K, prebuilt in global memory, hot in L2) in 16 KB atoms, issued
-      // after the token boxes of the first MMA group so that their DRAM reads start first.
-      const int my_blocks = groups > static_cast<int>(blockIdx.x)
-                                ? (groups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                                      static_cast<int>(gridDim.x)
-                                : 0;
-      const int op_after = min(G, my_blocks);
-      bool op_issued = false;
-      auto issue_operand = [&]() {  // exactly once per CTA
-        if (op_issued) return;
-        op_issued = true;
-        mbar_arrive_expect_tx(aready, rp.a_bytes);
-        for (uint32_t off = 0; off < rp.a_bytes; off += 16384u)
-          bulk_load_g2s(a_base + off, rp.a_op + off, 16384u, aready);
-      };
-      int n = 0;
+      int n = n_pre;
       bool ok = true;
-      for (int g = blockIdx.x; g < groups; g += gridDim.x, ++n) {
-        if (n == op_after) issue_operand();
+      for (int g = static_cast<int>(blockIdx.x) + n * static_cast<int>(gridDim.x); g < groups; g += gridDim.x, ++n) {
         const int s = n % ns;
-        if (n >= ns && !mbar_wait(&empty[s], ((n / ns) & 1u) ^ 1u, abort_flag)) {
+        if (!mbar_wait(&empty[s], ((n / ns) & 1u) ^ 1u, abort_flag)) {  // n >= ns: the stage was used
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&full[s], rp.stage_bytes);
         tma_load_3d(b_base + s * rp.stage_bytes, &tmX, &full[s], 0, 0, g * P);
       }
-      issue_operand();  // when every block of this CTA was issued first (or none exist, or on abort)
       if (!ok) {  // let the copies already issued land before the CTA can exit
         mbar_wait(aready, 0, nullptr);
         for (int j = n > ns ? n - ns : 0; j < n; ++j) mbar_wait(&full[j % ns], (j / ns) & 1u, nullptr);
@@ -318,10 +318,6 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16_bmn(128, 64 * G);
       const uint32_t a0 = smem_u32(a_base);
-      const int my_blocks = groups > static_cast<int>(blockIdx.x)
-                                ? (groups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                                      static_cast<int>(gridDim.x)
-                                : 0;
       bool ok = mbar_wait(aready, 0, abort_flag);
       for (int q = 0; ok && q * G < my_blocks; ++q) {
         const int slot = q % S, use = q / S, n0 = q * G;
@@ -369,10 +365,6 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
     const int bar_cnt = tw * 32;
     float* rmax = red_max + team * 16;
     int* rsum = red_sum + team * 16;
-    const int my_blocks = groups > static_cast<int>(blockIdx.x)
-                              ? (groups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                                    static_cast<int>(gridDim.x)
-                              : 0;
     int it = 0;
     // split: all teams walk every group and team t takes block t of it (the group's TMEM slot is
     // freed once every team has loaded its block); otherwise team t takes groups t, t + nteam, ...
