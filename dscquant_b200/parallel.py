@@ -16,10 +16,13 @@ Exchange of the blocks (the only cross-device step):
   the GEMM epilogue of every rank stores each output tile into the output
   buffer of *every* rank at its column offset (dscq_matmul_cols with the peers'
   pointers: plain stores over NVLink), so the all-gather happens tile by tile
-  inside the GEMM and no transpose pass is needed. Three symmetric-memory
+  inside the GEMM and no transpose pass is needed. The GEMM runs in two parts:
+  first over this rank's own token rows, right after it quantised them, while a
+  side stream waits for the peers' row blocks and copies them in; then over the
+  gathered rows (one launch per contiguous range). Three symmetric-memory
   barriers per call: before the quantisation (no rank overwrites a buffer a
-  peer is still reading), after it (all row blocks written) and after the GEMM
-  (all output blocks landed).
+  peer is still reading), after it (all row blocks written; on the side stream)
+  and after the GEMM (all output blocks landed).
 * ``nccl``: local [M, N/p] block, ``all_gather_into_tensor`` into [p, M, N/p],
   then one copy into the [M, N] layout.
 
@@ -94,8 +97,9 @@ class ColumnParallelQuantLinear:
             g = group if group is not None else dist.group.WORLD
             self.out = symm_mem.empty((max_tokens, N), dtype=torch.bfloat16, device=self.device)
             self.hdl = symm_mem.rendezvous(self.out, g)
-            ptrs = list(self.hdl.buffer_ptrs)
-            self.peer_ptrs = (ctypes.c_void_p * len(ptrs))(*ptrs)
+            self.peer_base = [int(p) for p in self.hdl.buffer_ptrs]
+            self.side = torch.cuda.Stream(self.device)
+            self.gathered = torch.cuda.Event()
             # quantised activations: each rank writes its own token rows, then reads the others'
             self.a_sym = symm_mem.empty((max_tokens, self.KP // 2), dtype=torch.uint8, device=self.device)
             self.a_hdl = symm_mem.rendezvous(self.a_sym, g)
@@ -132,41 +136,58 @@ class ColumnParallelQuantLinear:
             return y
         if M > self.max_tokens:
             raise RuntimeError(f"M={M} exceeds max_tokens={self.max_tokens} of the symmetric output buffer")
-        q = self._quantize_rows_sharded(x.contiguous(), M)
-        rc = _lib.load().dscq_matmul_cols(ops._ptr(q[0]), ops._ptr(self.w_packed), ops._ptr(q[1]), None,
-                                         ops._ptr(self.sw), None, ops._ptr(self.bias), None, M, self.hi - self.lo,
-                                         self.KP, _lib.BF16, self.peer_ptrs, self.world, self.N, self.lo, 0,
-                                         ops._stream(self.device))
-        _lib.check(rc, "dscq_matmul_cols")
-        self._mark("gemm_peer_stores")
+        main = torch.cuda.current_stream(self.device)
+        self.hdl.barrier(channel=0)  # every rank is done reading last call's buffers
+        self._mark("barrier_in")
+        lo, hi = row_bounds(M, self.world, self.rank)
+        self._quantize_own_rows(x.contiguous(), lo, hi)
+        self._mark("quantize_rows")
+        # side stream: wait for every rank's row block, then copy the peers' rows in over NVLink
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            self.hdl.barrier(channel=1)
+            for r in range(self.world):
+                if r == self.rank:
+                    continue
+                rlo, rhi = row_bounds(M, self.world, r)
+                if rhi > rlo:
+                    self.a_sym[rlo:rhi].copy_(self.a_peer[r][rlo:rhi], non_blocking=True)
+                    self.s_sym[rlo:rhi].copy_(self.s_peer[r][rlo:rhi], non_blocking=True)
+        self.gathered.record(self.side)
+        # main stream: this rank's own rows first, then the gathered ones
+        self._gemm_rows(lo, hi)
+        self._mark("gemm_own_rows")
+        main.wait_event(self.gathered)
+        self._mark("gather_wait")
+        for r0, r1 in ((0, lo), (hi, M)):
+            self._gemm_rows(r0, r1)
+        self._mark("gemm_peer_rows")
         self.hdl.barrier(channel=2)
         self._mark("barrier_out")
         return self.out[:M].clone() if self.copy_out else self.out[:M]
 
-    def _quantize_rows_sharded(self, x: torch.Tensor, M: int):
+    def _gemm_rows(self, r0: int, r1: int) -> None:
+        """Token rows [r0, r1) of the gathered activations times this rank's weight shard, each output
+        tile stored into rows [r0, r1) of every rank's output buffer at this rank's column offset."""
+        if r1 <= r0:
+            return
+        row_off = r0 * self.N * 2  # bytes into each rank's [max_tokens, N] bf16 buffer
+        outs = (ctypes.c_void_p * self.world)(*[p + row_off for p in self.peer_base])
+        rc = _lib.load().dscq_matmul_cols(ops._ptr(self.a_sym[r0:r1]), ops._ptr(self.w_packed),
+                                         ops._ptr(self.s_sym[r0:r1]), None, ops._ptr(self.sw), None,
+                                         ops._ptr(self.bias), None, r1 - r0, self.hi - self.lo, self.KP, _lib.BF16,
+                                         outs, self.world, self.N, self.lo, 0, ops._stream(self.device))
+        _lib.check(rc, "dscq_matmul_cols")
+
+    def _quantize_own_rows(self, x: torch.Tensor, lo: int, hi: int) -> None:
         """Fused mode: rank r rotates and quantises token rows row_bounds(M, p, r) into its symmetric
-        buffers, then copies the other ranks' packed rows and scales over NVLink (peer reads), so every
-        rank holds the full packed activations after 1/p of the quantisation work."""
-        self.hdl.barrier(channel=0)  # every rank is done reading last call's buffers
-        self._mark("barrier_in")
-        lo, hi = row_bounds(M, self.world, self.rank)
-        if hi > lo:
-            a, h = self.h_rot
-            rows = x[lo:hi]
-            rc = _lib.load().dscq_rowquant(ops._ptr(rows), _lib.BF16, hi - lo, self.K, x.stride(0), int(self.rotate), a,
-                                          ops._ptr(h), _lib.ACT_SYM, 1.0, hi - lo, self.KP,
-                                          ops._ptr(self.a_sym[lo:hi]), self.KP // 2, ops._ptr(self.s_sym[lo:hi]),
-                                          None, None, None, 0, ops._stream(self.device))
-            _lib.check(rc, "rowquant")
-        self._mark("quantize_rows")
-        self.hdl.barrier(channel=1)  # all row blocks written
-        self._mark("barrier_rows")
-        for r in range(self.world):
-            if r == self.rank:
-                continue
-            rlo, rhi = row_bounds(M, self.world, r)
-            if rhi > rlo:
-                self.a_sym[rlo:rhi].copy_(self.a_peer[r][rlo:rhi], non_blocking=True)
-                self.s_sym[rlo:rhi].copy_(self.s_peer[r][rlo:rhi], non_blocking=True)
-        self._mark("gather_rows")
-        return self.a_sym, self.s_sym
+        buffers (the peers copy them from there)."""
+        if hi <= lo:
+            return
+        a, h = self.h_rot
+        rows = x[lo:hi]
+        rc = _lib.load().dscq_rowquant(ops._ptr(rows), _lib.BF16, hi - lo, self.K, x.stride(0), int(self.rotate), a,
+                                      ops._ptr(h), _lib.ACT_SYM, 1.0, hi - lo, self.KP,
+                                      ops._ptr(self.a_sym[lo:hi]), self.KP // 2, ops._ptr(self.s_sym[lo:hi]),
+                                      None, None, None, 0, ops._stream(self.device))
+        _lib.check(rc, "rowquant")
