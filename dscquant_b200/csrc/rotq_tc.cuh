@@ -143,14 +143,19 @@ __device__ __forceinline__ void wht64_regs(float2 (&u)[32]) {
       }
 }
 
+// Three-operand f32 max (sm_100): half the max instructions of a two-operand chain.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// max |u| over the 64 values, four independent chains of three-operand maxima.
 __device__ __forceinline__ float absmax64(const float2 (&u)[32]) {
-  float m0 = 0.f, m1 = 0.f;
+  float m[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    m0 = fmaxf(m0, fabsf(u[i].x));
-    m1 = fmaxf(m1, fabsf(u[i].y));
-  }
-  return fmaxf(m0, m1);
+  for (int i = 0; i < 32; ++i) m[i & 3] = fmax3(m[i & 3], fabsf(u[i].x), fabsf(u[i].y));
+  return fmax3(fmaxf(m[0], m[1]), m[2], m[3]);
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
