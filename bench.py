@@ -494,10 +494,12 @@ def layer_from_sweep(sweep, layer, input_k):
 # ---------------------------------------------------------------- config 4: Llama-2-70B layer, column-parallel
 def tp70_record(dev, rank: int, world: int, steps: int = 10, warmup: int = 3) -> dict:
     """The five Llama-2-70B layer linears at M = 4096, output channels split over the `world` ranks of the
-    job (strong scaling: the total work is fixed). N = 1: one GPU, no exchange. N > 1: both exchange modes
-    of parallel.ColumnParallelQuantLinear -- 'fused' (row-split quantisation into symmetric memory, peer
-    reads of the other ranks' rows, GEMM epilogue storing every tile into every rank's output over
-    NVLink) and 'nccl' (replicated quantisation, local GEMM, NCCL all-gather, reassembly). Times are CUDA
+    job (strong scaling: the total work is fixed). N = 1: one GPU, no exchange. N > 1: the three exchange
+    modes of parallel.ColumnParallelQuantLinear -- 'fused' (row-split quantisation into symmetric memory,
+    peer reads of the other ranks' rows, GEMM epilogue storing every tile into every rank's output over
+    NVLink), 'push' (the same, the epilogue storing locally and a row-block copy pushing each finished
+    block to the peers beside the next GEMM launch) and 'nccl' (replicated quantisation, local GEMM,
+    NCCL all-gather, reassembly); `value` is the best of them. Times are CUDA
     events on each rank's stream, max over ranks; per-phase milliseconds per step from events recorded
     at the phase boundaries of every call (max over ranks)."""
     import torch
@@ -550,7 +552,7 @@ def tp70_record(dev, rank: int, world: int, steps: int = 10, warmup: int = 3) ->
         rec["single"] = {"ms_per_step": ms, "value": ops_total / (ms * 1e-3) / 1e12}
         rec["value"] = rec["single"]["value"]
         return rec
-    for mode in ("fused", "nccl"):
+    for mode in ("fused", "push", "nccl"):
         layers = []
         for i, (name, K, N) in enumerate(LAYER70):
             lo, hi = parallel.shard_bounds(N, world, rank)
@@ -586,7 +588,8 @@ def tp70_record(dev, rank: int, world: int, steps: int = 10, warmup: int = 3) ->
         del layers
         torch.cuda.synchronize(dev)
         torch.distributed.barrier()
-    rec["value"] = max(rec["fused"]["value"], rec["nccl"]["value"])
+    rec["value"] = max(rec[m]["value"] for m in ("fused", "push", "nccl"))
+    rec["best_mode"] = max(("fused", "push", "nccl"), key=lambda m: rec[m]["value"])
     return rec
 
 

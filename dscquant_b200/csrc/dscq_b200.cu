@@ -26,6 +26,7 @@
 #include "headrot_quant.cuh"
 #include "rotq_tc.cuh"
 #include "llama_ops.cuh"
+#include "scatter_block.cuh"
 
 namespace {
 
@@ -877,6 +878,36 @@ int dscq_matmul_cols(const uint8_t* a, const uint8_t* b, const float* sx, const 
   DSCQ_REQUIRE(outs != nullptr && n_outs >= 1, "need at least one output buffer");
   return matmul_impl(a, b, sx, zx, sw, sums, bias, residual, M, N, KP, out_dtype, outs, n_outs, ld_out, col_off,
                      nullptr, variant, stream);
+}
+
+int dscq_scatter_block(const void* src, int64_t ld_src, int64_t rows, int64_t width, void* const* dsts, int n_dst,
+                       int64_t ld_dst, void* stream) {
+  DSCQ_REQUIRE(src != nullptr && dsts != nullptr && n_dst >= 1 && n_dst <= 8, "need a source and 1..8 destinations");
+  DSCQ_REQUIRE(rows >= 0 && width >= 0 && width % 16 == 0, "width must be a non-negative multiple of 16 bytes");
+  DSCQ_REQUIRE(ld_src % 16 == 0 && ld_dst % 16 == 0 && ld_src >= width && ld_dst >= width,
+               "row strides must be multiples of 16 bytes and cover the width");
+  DSCQ_REQUIRE(aligned(src, 16), "source must be 16-byte aligned");
+  dscq::ScatterParams p{};
+  p.src = static_cast<const uint8_t*>(src);
+  p.ld_src = ld_src;
+  p.ld_dst = ld_dst;
+  p.rows = rows;
+  p.width = width;
+  p.n_dst = n_dst;
+  for (int i = 0; i < n_dst; ++i) {
+    DSCQ_REQUIRE(dsts[i] != nullptr && aligned(dsts[i], 16), "destinations must be non-null and 16-byte aligned");
+    p.dst[i] = static_cast<uint8_t*>(dsts[i]);
+  }
+  if (rows == 0 || width == 0) return DSCQ_OK;
+  int st = check_device(nullptr);
+  if (st) return st;
+  const int64_t units = ((rows + 7) / 8) * ((width + 63) / 64);
+  const int64_t want = (units + 3) / 4;  // 4 warps per CTA
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, 4 * num_sms())));
+  dscq::scatter_block_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch scatter_block");
+  return DSCQ_OK;
 }
 
 int dscq_matmul_a8(const int8_t* a, int64_t ld_a, const uint8_t* b, const float* sx, const float* sw, const void* bias,

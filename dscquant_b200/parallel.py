@@ -23,6 +23,11 @@ Exchange of the blocks (the only cross-device step):
   barriers per call: before the quantisation (no rank overwrites a buffer a
   peer is still reading), after it (all row blocks written; on the side stream)
   and after the GEMM (all output blocks landed).
+* ``push``: as ``fused``, but each GEMM launch stores only into this rank's own
+  buffer, and dscq_scatter_block then copies the finished row block into the
+  peers' buffers on a second side stream, beside the next GEMM launch. Remote
+  stores from the epilogue stall the accumulator pipeline once a rank writes to
+  several peers; as a separate copy they do not.
 * ``nccl``: local [M, N/p] block, ``all_gather_into_tensor`` into [p, M, N/p],
   then one copy into the [M, N] layout.
 
@@ -71,8 +76,8 @@ class ColumnParallelQuantLinear:
 
     def __init__(self, weight_shard: torch.Tensor, N: int, group=None, rotate: bool = True, mode: str = "fused",
                  max_tokens: int = 8192, bias_shard: torch.Tensor | None = None, copy_out: bool = True):
-        if mode not in ("fused", "nccl"):
-            raise ValueError("mode must be 'fused' or 'nccl'")
+        if mode not in ("fused", "push", "nccl"):
+            raise ValueError("mode must be 'fused', 'push' or 'nccl'")
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -80,6 +85,8 @@ class ColumnParallelQuantLinear:
         self.lo, self.hi = shard_bounds(N, self.world, self.rank)
         if weight_shard.shape[0] != self.hi - self.lo:
             raise ValueError("weight_shard must hold this rank's N/p output channels")
+        if mode == "push" and (self.lo % 8 or (self.hi - self.lo) % 8):
+            raise ValueError("push mode needs column blocks of a multiple of 8 channels (16-byte rows)")
         self.K = weight_shard.shape[1]
         self.KP = (self.K + 63) // 64 * 64
         self.rotate = rotate
@@ -91,7 +98,7 @@ class ColumnParallelQuantLinear:
         self.w_packed, self.sw = q.packed, q.scales
         self.bias = None if bias_shard is None else bias_shard.to(torch.bfloat16).contiguous()
         self.max_tokens = max_tokens
-        if mode == "fused":
+        if mode in ("fused", "push"):
             import torch.distributed._symmetric_memory as symm_mem
 
             g = group if group is not None else dist.group.WORLD
@@ -100,6 +107,9 @@ class ColumnParallelQuantLinear:
             self.peer_base = [int(p) for p in self.hdl.buffer_ptrs]
             self.side = torch.cuda.Stream(self.device)
             self.gathered = torch.cuda.Event()
+            self.peer_rows_in = [torch.cuda.Event() for _ in range(self.world)]
+            self.push_stream = torch.cuda.Stream(self.device)
+            self.block_done = [torch.cuda.Event() for _ in range(self.world)]
             # quantised activations: each rank writes its own token rows, then reads the others'
             self.a_sym = symm_mem.empty((max_tokens, self.KP // 2), dtype=torch.uint8, device=self.device)
             self.a_hdl = symm_mem.rendezvous(self.a_sym, g)
@@ -142,7 +152,8 @@ class ColumnParallelQuantLinear:
         lo, hi = row_bounds(M, self.world, self.rank)
         self._quantize_own_rows(x.contiguous(), lo, hi)
         self._mark("quantize_rows")
-        # side stream: wait for every rank's row block, then copy the peers' rows in over NVLink
+        # side stream: wait for every rank's row block, then copy the peers' rows in over NVLink, one
+        # event per peer block so that the GEMM on a block can start as soon as that block is in
         self.side.wait_stream(main)
         with torch.cuda.stream(self.side):
             self.hdl.barrier(channel=1)
@@ -153,31 +164,63 @@ class ColumnParallelQuantLinear:
                 if rhi > rlo:
                     self.a_sym[rlo:rhi].copy_(self.a_peer[r][rlo:rhi], non_blocking=True)
                     self.s_sym[rlo:rhi].copy_(self.s_peer[r][rlo:rhi], non_blocking=True)
+                self.peer_rows_in[r].record(self.side)
         self.gathered.record(self.side)
         # main stream: this rank's own rows first, then the gathered ones
-        self._gemm_rows(lo, hi)
+        push = self.mode == "push"
+        self._gemm_rows(lo, hi, local_only=push)
+        if push:
+            self._push_rows(main, 0, lo, hi)
         self._mark("gemm_own_rows")
-        main.wait_event(self.gathered)
-        self._mark("gather_wait")
-        for r0, r1 in ((0, lo), (hi, M)):
-            self._gemm_rows(r0, r1)
+        if push:  # one launch per peer's row block once it is in, each pushed as soon as it is done
+            for i, r in enumerate(r for r in range(self.world) if r != self.rank):
+                rlo, rhi = row_bounds(M, self.world, r)
+                main.wait_event(self.peer_rows_in[r])
+                self._gemm_rows(rlo, rhi, local_only=True)
+                self._push_rows(main, 1 + i, rlo, rhi)
+        else:
+            main.wait_event(self.gathered)
+            for r0, r1 in ((0, lo), (hi, M)):
+                self._gemm_rows(r0, r1)
         self._mark("gemm_peer_rows")
+        if push:
+            main.wait_stream(self.push_stream)
+            self._mark("push_wait")
         self.hdl.barrier(channel=2)
         self._mark("barrier_out")
         return self.out[:M].clone() if self.copy_out else self.out[:M]
 
-    def _gemm_rows(self, r0: int, r1: int) -> None:
+    def _gemm_rows(self, r0: int, r1: int, local_only: bool = False) -> None:
         """Token rows [r0, r1) of the gathered activations times this rank's weight shard, each output
-        tile stored into rows [r0, r1) of every rank's output buffer at this rank's column offset."""
+        tile stored into rows [r0, r1) at this rank's column offset of every rank's output buffer (or of
+        this rank's only, with local_only)."""
         if r1 <= r0:
             return
         row_off = r0 * self.N * 2  # bytes into each rank's [max_tokens, N] bf16 buffer
-        outs = (ctypes.c_void_p * self.world)(*[p + row_off for p in self.peer_base])
+        bases = [self.peer_base[self.rank]] if local_only else self.peer_base
+        outs = (ctypes.c_void_p * len(bases))(*[p + row_off for p in bases])
         rc = _lib.load().dscq_matmul_cols(ops._ptr(self.a_sym[r0:r1]), ops._ptr(self.w_packed),
                                          ops._ptr(self.s_sym[r0:r1]), None, ops._ptr(self.sw), None,
                                          ops._ptr(self.bias), None, r1 - r0, self.hi - self.lo, self.KP, _lib.BF16,
-                                         outs, self.world, self.N, self.lo, 0, ops._stream(self.device))
+                                         outs, len(bases), self.N, self.lo, 0, ops._stream(self.device))
         _lib.check(rc, "dscq_matmul_cols")
+
+    def _push_rows(self, main, k: int, r0: int, r1: int) -> None:
+        """Push mode: once the main stream's GEMM launch for rows [r0, r1) is done, copy this rank's columns
+        of those rows from its own output buffer into every peer's (push stream, beside the next GEMM)."""
+        peers = [r for r in range(self.world) if r != self.rank]
+        if r1 <= r0 or not peers:
+            return
+        ev = self.block_done[k]
+        ev.record(main)
+        self.push_stream.wait_event(ev)
+        ld = self.N * 2
+        off = r0 * ld + self.lo * 2
+        dsts = (ctypes.c_void_p * len(peers))(*[self.peer_base[r] + off for r in peers])
+        rc = _lib.load().dscq_scatter_block(ctypes.c_void_p(self.peer_base[self.rank] + off), ld, r1 - r0,
+                                           (self.hi - self.lo) * 2, dsts, len(peers), ld,
+                                           ctypes.c_void_p(self.push_stream.cuda_stream))
+        _lib.check(rc, "dscq_scatter_block")
 
     def _quantize_own_rows(self, x: torch.Tensor, lo: int, hi: int) -> None:
         """Fused mode: rank r rotates and quantises token rows row_bounds(M, p, r) into its symmetric

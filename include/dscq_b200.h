@@ -184,6 +184,18 @@ int dscq_matmul_cols(const uint8_t* a, const uint8_t* b, const float* sx, const 
                      void* stream);
 
 /*
+ * Row-block copy into several buffers (no counterpart in the reference, which
+ * has no multi-GPU code): rows x width bytes from `src` (row stride ld_src
+ * bytes) to each of the n_dst (1..8) buffers in `dsts` (row stride ld_dst
+ * bytes), same offsets. In a column-parallel group this pushes the columns a
+ * GPU computed into every peer's output buffer after the GEMM stored them
+ * locally; launched on a side stream it overlaps the next GEMM launch.
+ * Addresses and strides 16-byte aligned, width a multiple of 16.
+ */
+int dscq_scatter_block(const void* src, int64_t ld_src, int64_t rows, int64_t width, void* const* dsts, int n_dst,
+                       int64_t ld_dst, void* stream);
+
+/*
  * dscq_rowquant's tcgen05 rotate+quantize without any device allocation. No counterpart in the
  * reference: it exists for callers that cannot call cudaMalloc, such as serving engines that
  * reserve all device memory up front for weights and KV cache and allocate only from their own

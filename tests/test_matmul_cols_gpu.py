@@ -74,3 +74,43 @@ def test_matmul_cols_argument_checks(cuda_device):
     assert lib.dscq_matmul_cols(*args, ptrs, 0, 2 * N, 0, 0, st) == _lib.DSCQ_ERR_INVALID      # no buffer
     nine = (ctypes.c_void_p * 9)(*([out.data_ptr()] * 9))
     assert lib.dscq_matmul_cols(*args, nine, 9, 2 * N, 0, 0, st) == _lib.DSCQ_ERR_INVALID      # > 8 buffers
+
+
+@pytest.mark.parametrize("rows,width_cols,col_off", [(1, 8, 0), (300, 512, 512), (2048, 5120, 1024), (7, 24, 8)])
+def test_scatter_block_copies_the_block_only(cuda_device, rows, width_cols, col_off):
+    """dscq_scatter_block: rows x width of a bf16 buffer (row stride ld) land at the same offsets of every
+    destination buffer, and nothing else in them changes."""
+    from dscquant_b200 import _lib, ops
+
+    ld = col_off + width_cols + 40
+    g = torch.Generator(device=cuda_device).manual_seed(rows + width_cols)
+    src = torch.randn((rows, ld), generator=g, device=cuda_device).to(torch.bfloat16)
+    sentinel = -777.0
+    dsts = [torch.full((rows, ld), sentinel, dtype=torch.bfloat16, device=cuda_device) for _ in range(3)]
+    off = col_off * 2
+    ptrs = (ctypes.c_void_p * 3)(*[t.data_ptr() + off for t in dsts])
+    lib = _lib.load()
+    rc = lib.dscq_scatter_block(ctypes.c_void_p(src.data_ptr() + off), ld * 2, rows, width_cols * 2, ptrs, 3, ld * 2,
+                                ops._stream(cuda_device))
+    _lib.check(rc, "dscq_scatter_block")
+    torch.cuda.synchronize()
+    for t in dsts:
+        assert torch.equal(t[:, col_off:col_off + width_cols], src[:, col_off:col_off + width_cols])
+        outside = torch.cat([t[:, :col_off], t[:, col_off + width_cols:]], dim=1)
+        assert bool((outside == sentinel).all())
+    assert ops.device_status(cuda_device) == 0
+
+
+def test_scatter_block_argument_checks(cuda_device):
+    from dscquant_b200 import _lib, ops
+
+    buf = torch.zeros((4, 64), dtype=torch.bfloat16, device=cuda_device)
+    lib = _lib.load()
+    one = (ctypes.c_void_p * 1)(buf.data_ptr())
+    st = ops._stream(cuda_device)
+    src = ctypes.c_void_p(buf.data_ptr())
+    assert lib.dscq_scatter_block(src, 128, 4, 24, one, 1, 128, st) == _lib.DSCQ_ERR_INVALID  # width % 16
+    assert lib.dscq_scatter_block(src, 128, 4, 144, one, 1, 128, st) == _lib.DSCQ_ERR_INVALID  # width > ld
+    assert lib.dscq_scatter_block(src, 128, 4, 64, one, 0, 128, st) == _lib.DSCQ_ERR_INVALID  # no destination
+    nine = (ctypes.c_void_p * 9)(*([buf.data_ptr()] * 9))
+    assert lib.dscq_scatter_block(src, 128, 4, 64, nine, 9, 128, st) == _lib.DSCQ_ERR_INVALID  # > 8

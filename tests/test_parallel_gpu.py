@@ -1,5 +1,6 @@
-"""Column-parallel W4A4 linear on 2 GPUs (NCCL + symmetric memory): the gathered [M, N] output of both
-exchange modes (all-gather fused into the GEMM epilogue over NVLink, and NCCL all-gather) is
+"""Column-parallel W4A4 linear on 2 GPUs (NCCL + symmetric memory): the gathered [M, N] output of every
+exchange mode (all-gather fused into the GEMM epilogue over NVLink, local epilogue plus a pushed row-block
+copy, and NCCL all-gather) is
 bit-identical to a single-GPU QuantLinear on the full weight, also when two consecutive results are
 held at once. Skipped when fewer than 2 GPUs exist."""
 import os
@@ -51,7 +52,7 @@ def _worker(rank, world, port, q):
         ref2 = ql(x2)
         lo, hi = parallel.shard_bounds(N, world, rank)
         ok = []
-        for mode in ("fused", "nccl"):
+        for mode in ("fused", "push", "nccl"):
             layer = parallel.ColumnParallelQuantLinear(w[lo:hi], N, mode=mode, max_tokens=512)
             # two results held at once: the second call reuses the symmetric buffer, and the first
             # result (a copy by default) must keep its values
@@ -80,4 +81,4 @@ def test_column_parallel_matches_single_gpu():
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs)
     results = dict(q.get(timeout=5) for _ in range(world))
-    assert results[0] == [True, True] and results[1] == [True, True]
+    assert results[0] == [True] * 3 and results[1] == [True] * 3  # fused, push, nccl
