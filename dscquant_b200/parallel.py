@@ -9,7 +9,7 @@ bit-identical to the same columns of a single-GPU QuantLinear.
 
 Exchange of the blocks (the only cross-device step):
 
-* ``fused`` (default): the input rows are split across the ranks for the
+* ``fused`` (``auto`` at 2 GPUs): the input rows are split across the ranks for the
   rotate+quantize (each rank quantises M/p token rows into a symmetric buffer
   and then copies the other ranks' packed rows and scales over NVLink), and the
   [M, N] output lives in symmetric memory (torch.distributed._symmetric_memory):
@@ -23,7 +23,7 @@ Exchange of the blocks (the only cross-device step):
   barriers per call: before the quantisation (no rank overwrites a buffer a
   peer is still reading), after it (all row blocks written; on the side stream)
   and after the GEMM (all output blocks landed).
-* ``push``: as ``fused``, but each GEMM launch stores only into this rank's own
+* ``push`` (``auto`` from 3 GPUs): as ``fused``, but each GEMM launch stores only into this rank's own
   buffer, and dscq_scatter_block then copies the finished row block into the
   peers' buffers on a second side stream, beside the next GEMM launch. Remote
   stores from the epilogue stall the accumulator pipeline once a rank writes to
@@ -74,13 +74,15 @@ def assemble(blocks: torch.Tensor) -> torch.Tensor:
 class ColumnParallelQuantLinear:
     """W4A4 y = x W^T with W's output channels split across the ranks of `group`."""
 
-    def __init__(self, weight_shard: torch.Tensor, N: int, group=None, rotate: bool = True, mode: str = "fused",
+    def __init__(self, weight_shard: torch.Tensor, N: int, group=None, rotate: bool = True, mode: str = "auto",
                  max_tokens: int = 8192, bias_shard: torch.Tensor | None = None, copy_out: bool = True):
-        if mode not in ("fused", "push", "nccl"):
-            raise ValueError("mode must be 'fused', 'push' or 'nccl'")
+        if mode not in ("auto", "fused", "push", "nccl"):
+            raise ValueError("mode must be 'auto', 'fused', 'push' or 'nccl'")
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        if mode == "auto":  # measured on B200: epilogue stores win at 2 GPUs, pushed blocks from 4
+            mode = "fused" if self.world <= 2 else "push"
         self.N = N
         self.lo, self.hi = shard_bounds(N, self.world, self.rank)
         if weight_shard.shape[0] != self.hi - self.lo:
