@@ -606,17 +606,26 @@ def prefill_record(dev, seq: int = 2048, reps: int = 5) -> dict:
         model(ids)
     torch.cuda.synchronize(dev)
     stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
-        logits = model(ids)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / reps
-    ok = bool(torch.isfinite(logits.float()).all())
+
+    def timed(fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            out = fn(ids)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps, out
+
+    ms_eager, logits = timed(model)
+    graph = model.graph(seq)  # the same kernels, replayed from one CUDA graph
+    graph(ids)
+    ms, glogits = timed(graph)
+    ok = bool(torch.isfinite(logits.float()).all()) and bool(torch.equal(glogits, logits))
+    del graph
     rec = {"workload": "llama2-7b-prefill", "batch": 1, "seq_len": seq, "layers": cfg.layers, "vocab": cfg.vocab,
-           "tokens_per_s": seq / (ms * 1e-3), "ms_per_prefill": ms, "reps": reps,
-           "w4a4_linear_tops": model.linear_ops(seq) / (ms * 1e-3) / 1e12, "logits_finite": ok,
+           "tokens_per_s": seq / (ms * 1e-3), "ms_per_prefill": ms, "reps": reps, "launch": "one CUDA graph",
+           "tokens_per_s_eager": seq / (ms_eager * 1e-3), "ms_per_prefill_eager": ms_eager,
+           "w4a4_linear_tops": model.linear_ops(seq) / (ms * 1e-3) / 1e12, "logits_finite_and_graph_equal": ok,
            "note": "all 224 projections + LM head W4A4 (rotate+quantize shared by q/k/v and by gate/up, residuals "
                    "added in the GEMM epilogue); RMSNorm / RoPE / SiLU-gate as single-pass bf16 kernels of this "
                    "package; causal attention bf16 torch SDPA; random-init weights, uniform random token ids"}

@@ -999,11 +999,19 @@ int dscq_rope(void* q, void* k, const void* cos_t, const void* sin_t, int64_t S,
   DSCQ_REQUIRE(S >= 1 && Hq >= 1 && Hk >= 1 && D >= 2 && D % 2 == 0 && D <= 1024, "invalid rope shape");
   int st = check_device(nullptr);
   if (st) return st;
-  const int64_t total = S * (Hq + Hk) * (D / 2);
+  const bool vec = (D / 2) % 8 == 0 && aligned(q, 16) && aligned(k, 16) && aligned(cos_t, 16) && aligned(sin_t, 16);
+  const int64_t total = S * (Hq + Hk) * (D / 2) / (vec ? 8 : 1);
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, int64_t(num_sms()) * 16));
-  dscq::rope_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(cos_t),
-      static_cast<const __nv_bfloat16*>(sin_t), static_cast<int>(S), Hq, Hk, D);
+  auto* qq = static_cast<__nv_bfloat16*>(q);
+  auto* kk = static_cast<__nv_bfloat16*>(k);
+  const auto* cc = static_cast<const __nv_bfloat16*>(cos_t);
+  const auto* ss = static_cast<const __nv_bfloat16*>(sin_t);
+  if (vec)
+    dscq::rope_vec_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(qq, kk, cc, ss, static_cast<int>(S), Hq,
+                                                                               Hk, D);
+  else
+    dscq::rope_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(qq, kk, cc, ss, static_cast<int>(S), Hq, Hk,
+                                                                           D);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch rope");
   return DSCQ_OK;

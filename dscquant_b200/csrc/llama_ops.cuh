@@ -78,6 +78,44 @@ __global__ void __launch_bounds__(256) rope_kernel(__nv_bfloat16* q, __nv_bfloat
   }
 }
 
+// The same rotation, eight consecutive pairs per thread with 16-byte loads and stores (D/2 a multiple of 8,
+// every row 16-byte aligned): one thread per (row, group of 8 j).
+__global__ void __launch_bounds__(256) rope_vec_kernel(__nv_bfloat16* q, __nv_bfloat16* k, const __nv_bfloat16* cs,
+                                                       const __nv_bfloat16* sn, int S, int Hq, int Hk, int D) {
+  const int half = D / 2, ng = half / 8;
+  const int64_t total = static_cast<int64_t>(S) * (Hq + Hk) * ng;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(t % ng) * 8;
+    const int64_t hr = t / ng;
+    const int s = static_cast<int>(hr / (Hq + Hk)), hh = static_cast<int>(hr % (Hq + Hk));
+    __nv_bfloat16* base = hh < Hq ? q + (static_cast<int64_t>(s) * Hq + hh) * D
+                                  : k + (static_cast<int64_t>(s) * Hk + (hh - Hq)) * D;
+    const __nv_bfloat16* c = cs + static_cast<int64_t>(s) * D;
+    const __nv_bfloat16* n = sn + static_cast<int64_t>(s) * D;
+    const uint4 vx1 = *reinterpret_cast<const uint4*>(base + j), vx2 = *reinterpret_cast<const uint4*>(base + j + half);
+    const uint4 vc1 = *reinterpret_cast<const uint4*>(c + j), vc2 = *reinterpret_cast<const uint4*>(c + j + half);
+    const uint4 vs1 = *reinterpret_cast<const uint4*>(n + j), vs2 = *reinterpret_cast<const uint4*>(n + j + half);
+    const __nv_bfloat16* x1 = reinterpret_cast<const __nv_bfloat16*>(&vx1);
+    const __nv_bfloat16* x2 = reinterpret_cast<const __nv_bfloat16*>(&vx2);
+    const __nv_bfloat16* c1 = reinterpret_cast<const __nv_bfloat16*>(&vc1);
+    const __nv_bfloat16* c2 = reinterpret_cast<const __nv_bfloat16*>(&vc2);
+    const __nv_bfloat16* s1 = reinterpret_cast<const __nv_bfloat16*>(&vs1);
+    const __nv_bfloat16* s2 = reinterpret_cast<const __nv_bfloat16*>(&vs2);
+    uint4 o1, o2;
+    __nv_bfloat16* y1 = reinterpret_cast<__nv_bfloat16*>(&o1);
+    __nv_bfloat16* y2 = reinterpret_cast<__nv_bfloat16*>(&o2);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float a = __bfloat162float(x1[e]), b = __bfloat162float(x2[e]);
+      y1[e] = __float2bfloat16_rn(bf16r(a * __bfloat162float(c1[e])) + bf16r(-b * __bfloat162float(s1[e])));
+      y2[e] = __float2bfloat16_rn(bf16r(b * __bfloat162float(c2[e])) + bf16r(a * __bfloat162float(s2[e])));
+    }
+    *reinterpret_cast<uint4*>(base + j) = o1;
+    *reinterpret_cast<uint4*>(base + j + half) = o2;
+  }
+}
+
 // y = bf16(bf16(silu(g)) * u) over n elements (n a multiple of 8, 16-byte aligned buffers).
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ g,
                                                        const __nv_bfloat16* __restrict__ u, __nv_bfloat16* y,

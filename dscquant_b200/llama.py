@@ -145,9 +145,39 @@ class LlamaW4A4:
         x = ops.rmsnorm(h, self.norm, self.cfg.eps)
         return self.lm_head.forward_quantized(self.lm_head.quantize_input(x), S)
 
+    def graph(self, S: int) -> "PrefillGraph":
+        """The prefill of S tokens captured once as a CUDA graph (see PrefillGraph)."""
+        return PrefillGraph(self, S)
+
     def linear_ops(self, S: int) -> float:
         """Integer ops of all W4A4 GEMMs of one prefill of S tokens (2 * S * N * K each)."""
         c = self.cfg
         kv = c.kv_heads * c.head_dim
         per_layer = 2 * S * (c.hidden * c.hidden * 2 + 2 * kv * c.hidden + 3 * c.intermediate * c.hidden)
         return float(per_layer * c.layers + 2 * S * c.vocab * c.hidden)
+
+
+class PrefillGraph:
+    """One CUDA graph holding a whole prefill of S tokens: every kernel of __call__ (rotate+quantize,
+    W4A4 GEMMs, RMSNorm, RoPE, attention, SiLU gate, LM head) recorded once and replayed without the
+    host issuing each op. The ids are copied into a static buffer, and the logits come back in a
+    static buffer that the next replay overwrites. One eager pass runs first on a side stream: the
+    first call per device and K builds the rotate+quantize operand, which cannot be captured."""
+
+    def __init__(self, model: LlamaW4A4, S: int):
+        dev = model.device
+        self.ids = torch.zeros(S, dtype=torch.long, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            model(self.ids)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = model(self.ids)
+
+    def __call__(self, ids: torch.Tensor) -> torch.Tensor:
+        self.ids.copy_(ids)
+        self.graph.replay()
+        return self.logits

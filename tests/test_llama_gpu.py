@@ -37,6 +37,24 @@ def test_small_llama_prefill(cuda_device):
     assert model.linear_ops(96) > 0
 
 
+def test_prefill_graph_replay_matches_eager(cuda_device):
+    """The CUDA-graph prefill launches the same kernels: its logits equal the eager pass bit for bit, for
+    two different token sequences replayed from one graph."""
+    from dscquant_b200.llama import LlamaConfig, LlamaW4A4
+
+    cfg = LlamaConfig(vocab=512, hidden=1024, heads=8, kv_heads=4, intermediate=2048, layers=2)
+    model = LlamaW4A4(cfg, cuda_device, seed=3)
+    gen = torch.Generator(device=cuda_device).manual_seed(4)
+    g = model.graph(128)
+    for _ in range(2):
+        ids = torch.randint(0, cfg.vocab, (128,), device=cuda_device, generator=gen)
+        ref = model(ids)
+        out = g(ids).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    del g
+
+
 def test_prefill_elementwise_ops_match_torch(cuda_device):
     """ops.rmsnorm / rope_ / silu_mul against the torch expressions of the harness: RoPE bit-exact (same
     rounding steps); RMSNorm and the SiLU gate within one bf16 step (the row sum of squares, rsqrt and exp
@@ -60,6 +78,12 @@ def test_prefill_elementwise_ops_match_torch(cuda_device):
     rq, rk = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
     ops.rope_(q, k, cos, sin)
     assert torch.equal(q, rq) and torch.equal(k, rk)
+    cos2, sin2 = rope_tables(S, 24, 10000.0, cuda_device)  # D/2 = 12: the one-pair-per-thread kernel
+    q2 = torch.randn(S, 3, 24, generator=g, device=cuda_device).to(torch.bfloat16)
+    k2 = torch.randn(S, 2, 24, generator=g, device=cuda_device).to(torch.bfloat16)
+    rq2, rk2 = apply_rope(q2, cos2, sin2), apply_rope(k2, cos2, sin2)
+    ops.rope_(q2, k2, cos2, sin2)
+    assert torch.equal(q2, rq2) and torch.equal(k2, rk2)
     a = (torch.randn(S, 1000, generator=g, device=cuda_device) * 4).to(torch.bfloat16)
     b = torch.randn(S, 1000, generator=g, device=cuda_device).to(torch.bfloat16)
     ref = F.silu(a) * b
