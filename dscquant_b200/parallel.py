@@ -19,10 +19,11 @@ Exchange of the blocks (the only cross-device step):
   inside the GEMM and no transpose pass is needed. The GEMM runs in two parts:
   first over this rank's own token rows, right after it quantised them, while a
   side stream waits for the peers' row blocks and copies them in; then over the
-  gathered rows (one launch per contiguous range). Three symmetric-memory
-  barriers per call: before the quantisation (no rank overwrites a buffer a
-  peer is still reading), after it (all row blocks written; on the side stream)
-  and after the GEMM (all output blocks landed).
+  gathered rows (one launch per contiguous range). Two symmetric-memory
+  barriers per call: after the quantisation (all row blocks written; on the side
+  stream) and after the GEMM (all output blocks landed). The symmetric buffers
+  exist twice and alternate between calls, so no rank overwrites a buffer that a
+  peer may still be reading and no entry barrier is needed.
 * ``push`` (``auto`` from 3 GPUs): as ``fused``, but each GEMM launch stores only into this rank's own
   buffer, and dscq_scatter_block then copies the finished row block into the
   peers' buffers on a second side stream, beside the next GEMM launch. Remote
@@ -31,13 +32,13 @@ Exchange of the blocks (the only cross-device step):
 * ``nccl``: local [M, N/p] block, ``all_gather_into_tensor`` into [p, M, N/p],
   then one copy into the [M, N] layout.
 
-Result lifetime: both modes return a tensor the caller owns. In the fused mode
-the gathered output lives in the symmetric buffer, which the next call of the
-same layer overwrites from every rank's epilogue; the layer therefore returns a
-copy unless it was built with ``copy_out=False``. Then the returned tensor is a
-view of the symmetric buffer that stays valid only until the next call of this
-layer on any rank (a caller that consumes it before that call, as a layer stack
-does, saves the copy).
+Result lifetime: every mode returns a tensor the caller owns. In the fused and push
+modes the gathered output lives in a symmetric buffer that a later call of the same
+layer overwrites from every rank (the buffers alternate, so the second call after
+it); the layer therefore returns a copy unless it was built with ``copy_out=False``.
+Then the returned tensor is a view of the symmetric buffer that stays valid at least
+until the next call of this layer on any rank (a caller that consumes it before that
+call, as a layer stack does, saves the copy).
 """
 from __future__ import annotations
 
@@ -104,22 +105,36 @@ class ColumnParallelQuantLinear:
             import torch.distributed._symmetric_memory as symm_mem
 
             g = group if group is not None else dist.group.WORLD
-            self.out = symm_mem.empty((max_tokens, N), dtype=torch.bfloat16, device=self.device)
-            self.hdl = symm_mem.rendezvous(self.out, g)
-            self.peer_base = [int(p) for p in self.hdl.buffer_ptrs]
+            # Two copies of every symmetric buffer, used by alternate calls: a rank overwrites copy c only
+            # two calls after it last used it, and by then every peer has passed the intervening call's
+            # output barrier, so no entry barrier is needed.
+            self.out_all = symm_mem.empty((2, max_tokens, N), dtype=torch.bfloat16, device=self.device)
+            self.hdl = symm_mem.rendezvous(self.out_all, g)
+            self.peer_base_all = [int(p) for p in self.hdl.buffer_ptrs]
             self.side = torch.cuda.Stream(self.device)
             self.gathered = torch.cuda.Event()
             self.peer_rows_in = [torch.cuda.Event() for _ in range(self.world)]
             self.push_stream = torch.cuda.Stream(self.device)
             self.block_done = [torch.cuda.Event() for _ in range(self.world)]
             # quantised activations: each rank writes its own token rows, then reads the others'
-            self.a_sym = symm_mem.empty((max_tokens, self.KP // 2), dtype=torch.uint8, device=self.device)
-            self.a_hdl = symm_mem.rendezvous(self.a_sym, g)
-            self.s_sym = symm_mem.empty((max_tokens,), dtype=torch.float32, device=self.device)
-            self.s_hdl = symm_mem.rendezvous(self.s_sym, g)
-            self.a_peer = [self.a_hdl.get_buffer(r, (max_tokens, self.KP // 2), torch.uint8) for r in range(self.world)]
-            self.s_peer = [self.s_hdl.get_buffer(r, (max_tokens,), torch.float32) for r in range(self.world)]
+            self.a_all = symm_mem.empty((2, max_tokens, self.KP // 2), dtype=torch.uint8, device=self.device)
+            self.a_hdl = symm_mem.rendezvous(self.a_all, g)
+            self.s_all = symm_mem.empty((2, max_tokens), dtype=torch.float32, device=self.device)
+            self.s_hdl = symm_mem.rendezvous(self.s_all, g)
+            self.a_peer_all = [self.a_hdl.get_buffer(r, (2, max_tokens, self.KP // 2), torch.uint8)
+                               for r in range(self.world)]
+            self.s_peer_all = [self.s_hdl.get_buffer(r, (2, max_tokens), torch.float32) for r in range(self.world)]
+            self.calls = 0
+            self._select(0)
             self.h_rot = ops.rotation_factor(self.K, self.device) if rotate else (1, None)
+
+    def _select(self, c: int) -> None:
+        """Point the per-call views at copy c of the symmetric buffers."""
+        self.out = self.out_all[c]
+        self.peer_base = [p + c * self.max_tokens * self.N * 2 for p in self.peer_base_all]
+        self.a_sym, self.s_sym = self.a_all[c], self.s_all[c]
+        self.a_peer = [t[c] for t in self.a_peer_all]
+        self.s_peer = [t[c] for t in self.s_peer_all]
 
     def _mark(self, phase: str) -> None:
         if self.timeline is not None:
@@ -149,8 +164,8 @@ class ColumnParallelQuantLinear:
         if M > self.max_tokens:
             raise RuntimeError(f"M={M} exceeds max_tokens={self.max_tokens} of the symmetric output buffer")
         main = torch.cuda.current_stream(self.device)
-        self.hdl.barrier(channel=0)  # every rank is done reading last call's buffers
-        self._mark("barrier_in")
+        self._select(self.calls & 1)  # alternate buffer copies instead of an entry barrier
+        self.calls += 1
         lo, hi = row_bounds(M, self.world, self.rank)
         self._quantize_own_rows(x.contiguous(), lo, hi)
         self._mark("quantize_rows")
