@@ -552,6 +552,16 @@ def tp70_record(dev, rank: int, world: int, steps: int = 10, warmup: int = 3) ->
         rec["single"] = {"ms_per_step": ms, "value": ops_total / (ms * 1e-3) / 1e12}
         rec["value"] = rec["single"]["value"]
         return rec
+    # single-GPU result of the first linear (every rank holds the full weight for this check): every
+    # exchange mode's gathered [M, N] output must equal it bit for bit
+    _, K0, N0 = LAYER70[0]
+    gen.manual_seed(7000)
+    w0 = (torch.randn((N0, K0), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    qw0 = ops.rowquant(w0, "weight_sym", rotate=True, KP=K0)
+    qx0 = ops.rowquant(xs[K0], "act_sym", rotate=True, KP=K0)
+    y_ref = ops.w4a4_gemm(qx0.packed, qw0.packed, qx0.scales, qw0.scales, M=M, N=N0)
+    del w0, qw0, qx0
+    parity = {}
     for mode in ("fused", "push", "nccl"):
         layers = []
         for i, (name, K, N) in enumerate(LAYER70):
@@ -566,6 +576,9 @@ def tp70_record(dev, rank: int, world: int, steps: int = 10, warmup: int = 3) ->
                 layer(xs[K])
 
         ms = timed(step)
+        same = torch.tensor([1.0 if torch.equal(layers[0][1](xs[K0]), y_ref) else 0.0], device=dev)
+        torch.distributed.all_reduce(same, op=torch.distributed.ReduceOp.MIN)
+        parity[mode] = bool(same.item() == 1.0)
         # phase breakdown: one more instrumented pass of `steps` steps
         for _, layer in layers:
             layer.timeline = []
@@ -588,6 +601,7 @@ def tp70_record(dev, rank: int, world: int, steps: int = 10, warmup: int = 3) ->
         del layers
         torch.cuda.synchronize(dev)
         torch.distributed.barrier()
+    rec["bit_exact_vs_single_gpu"] = parity  # first linear, [4096, 10240], every rank
     rec["value"] = max(rec[m]["value"] for m in ("fused", "push", "nccl"))
     rec["best_mode"] = max(("fused", "push", "nccl"), key=lambda m: rec[m]["value"])
     return rec

@@ -43,6 +43,7 @@ SIGNATURES = {
                                       _vp]),
     "dscq_matmul_cols": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32,
                                 ctypes.POINTER(ctypes.c_void_p), _i32, _i64, _i64, _i32, _vp]),
+    "dscq_rowquant_auto_tc": (_i32, [_i64, _i64]),
     "dscq_scatter_block": (_i32, [_vp, _i64, _i64, _i64, ctypes.POINTER(ctypes.c_void_p), _i32, _i64, _vp]),
     "dscq_rowquant_tc_noalloc": (_i32, [_vp, _i32, _i64, _i64, _i64, _i32, _i32, _vp, _i32, _f32, _i64, _i64, _vp,
                                         _i64, _vp, _vp, _vp, _vp, _i64, _vp]),

@@ -284,6 +284,12 @@ int rotq_operand(int dev, int64_t K, const dscq::RotqParams& rp, const int8_t* h
   return DSCQ_OK;
 }
 
+// AUTO's choice of the tcgen05 rotate+quantize (a' = K / 64 rows of the dense factor): its longer fixed
+// prologue (TMEM, Hadamard operand) pays from 2048 rows, or from 1024 rows when a' > 64.
+bool rowquant_tc_auto(int ap_tc, int64_t rows) {
+  return ap_tc >= 32 && (rows >= 2048 || (ap_tc > 64 && rows >= 1024));
+}
+
 template <int MT, int G>
 cudaError_t launch_rotq(const CUtensorMap& tm, const dscq::RotqParams& rp, cudaStream_t st) {
   // at least 120 KB so that one CTA (which allocates all 512 TMEM columns) occupies an SM
@@ -473,6 +479,13 @@ int dscq_hadamard(int n, int8_t* out) {
   return DSCQ_OK;
 }
 
+int dscq_rowquant_auto_tc(int64_t K, int64_t rows) {
+  int aa = 0, lb = 0;
+  if (K < 1 || rows < 1 || !dscq::rotation_split(K, &aa, &lb)) return 0;
+  const int ap_tc = lb >= 6 ? static_cast<int>(K / 64) : 0;
+  return ap_tc >= 16 && ap_tc <= 224 && rowquant_tc_auto(ap_tc, rows) ? 1 : 0;
+}
+
 int dscq_rotation_split(int64_t K, int* a, int* b) {
   DSCQ_REQUIRE(a && b, "a and b must not be null");
   int aa = 0, lb = 0;
@@ -619,9 +632,7 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   if (variant == DSCQ_QUANT_TC && !tc_ok)
     return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize needs a rotation with K = a' * 64 (a' <= 224), a "
                                       "symmetric mode, bf16 input, KP == K and 16-byte aligned rows");
-  // AUTO: the tcgen05 kernel has a longer fixed prologue (TMEM, Hadamard operand) and wins once
-  // there is enough work: from 2048 rows, or from 1024 rows when the dense factor is larger than 64
-  const bool tc_auto = ap_tc >= 32 && (rows_out >= 2048 || (ap_tc > 64 && rows_out >= 1024));
+  const bool tc_auto = rowquant_tc_auto(ap_tc, rows_out);
   if (tc_ok && (variant == DSCQ_QUANT_TC || (variant == DSCQ_QUANT_AUTO && tc_auto))) {
     dscq::RotqParams rp;
     rp.p = p;

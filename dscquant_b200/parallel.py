@@ -240,14 +240,20 @@ class ColumnParallelQuantLinear:
         _lib.check(rc, "dscq_scatter_block")
 
     def _quantize_own_rows(self, x: torch.Tensor, lo: int, hi: int) -> None:
-        """Fused mode: rank r rotates and quantises token rows row_bounds(M, p, r) into its symmetric
-        buffers (the peers copy them from there)."""
+        """Fused and push modes: rank r rotates and quantises token rows row_bounds(M, p, r) into its
+        symmetric buffers (the peers copy them from there), with the kernel that one call on all M rows
+        would choose: the tcgen05 and CUDA-core quantizers may round a value at an exact tie differently,
+        and every rank's block must equal the single-GPU result bit for bit."""
         if hi <= lo:
             return
         a, h = self.h_rot
         rows = x[lo:hi]
-        rc = _lib.load().dscq_rowquant(ops._ptr(rows), _lib.BF16, hi - lo, self.K, x.stride(0), int(self.rotate), a,
-                                      ops._ptr(h), _lib.ACT_SYM, 1.0, hi - lo, self.KP,
-                                      ops._ptr(self.a_sym[lo:hi]), self.KP // 2, ops._ptr(self.s_sym[lo:hi]),
-                                      None, None, None, 0, ops._stream(self.device))
+        lib = _lib.load()
+        # the kernel a single call on all M rows would use, so the slice's codes are that call's
+        tc = self.rotate and lib.dscq_rowquant_auto_tc(self.K, x.shape[0]) == 1
+        rc = lib.dscq_rowquant_variant(ops._ptr(rows), _lib.BF16, hi - lo, self.K, x.stride(0), int(self.rotate), a,
+                                       ops._ptr(h), _lib.ACT_SYM, 1.0, hi - lo, self.KP,
+                                       ops._ptr(self.a_sym[lo:hi]), self.KP // 2, ops._ptr(self.s_sym[lo:hi]),
+                                       None, None, None, 0, _lib.QUANT_TC if tc else _lib.QUANT_LEGACY,
+                                       ops._stream(self.device))
         _lib.check(rc, "rowquant")

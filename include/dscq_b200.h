@@ -184,6 +184,17 @@ int dscq_matmul_cols(const uint8_t* a, const uint8_t* b, const float* sx, const 
                      void* stream);
 
 /*
+ * 1 if dscq_rowquant with DSCQ_QUANT_AUTO would take the tcgen05 rotate+quantize
+ * for `rows` rotated rows of length K (bf16, symmetric mode, 16-byte aligned),
+ * else 0. No counterpart in the reference. A caller that quantises a slice of
+ * a larger batch (the column-parallel layer quantises 1/p of the rows on each
+ * GPU) passes the whole batch's row count and forces the answer with
+ * dscq_rowquant_variant, so every slice gets the codes one call on the whole
+ * batch would give.
+ */
+int dscq_rowquant_auto_tc(int64_t K, int64_t rows);
+
+/*
  * Row-block copy into several buffers (no counterpart in the reference, which
  * has no multi-GPU code): rows x width bytes from `src` (row stride ld_src
  * bytes) to each of the n_dst (1..8) buffers in `dsts` (row stride ld_dst
