@@ -366,8 +366,10 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
     const int wtok = P > 1 ? (qd * 32) / ap16 : 0;  // lanes of a warp never straddle two tokens
     const int wpt = P > 1 ? ap16 / 32 : tw;        // team warps per token
     const int first_w = wtok * wpt;
-    const int bar_id = 1 + team;
-    const int bar_cnt = tw * 32;
+    // the warps of one token meet at their own named barrier (ids 1..8): with two tokens per block,
+    // each warp pair exchanges its row maximum without waiting for the team's other pair
+    const int bar_id = 1 + team * 2 + wtok;
+    const int bar_cnt = wpt * 32;
     float* rmax = red_max + team * 16;
     int* rsum = red_sum + team * 16;
     int it = 0;
