@@ -284,10 +284,13 @@ int rotq_operand(int dev, int64_t K, const dscq::RotqParams& rp, const int8_t* h
   return DSCQ_OK;
 }
 
-// AUTO's choice of the tcgen05 rotate+quantize (a' = K / 64 rows of the dense factor): its longer fixed
-// prologue (TMEM, Hadamard operand) pays from 2048 rows, or from 1024 rows when a' > 64.
+// AUTO's choice of the tcgen05 rotate+quantize (a' = K / 64 rows of the dense factor). With its
+// Hadamard operand prebuilt once per device and K it is as fast as the CUDA-core kernels or faster at
+// every row count measured (CUDA-graph replays on B200, 16 to 2048 rows: K = 4096 5.8 vs 6.0 us at
+// 16 rows and 11.5 vs 15.1 at 2048; K = 11008 6.2 vs 10.0 and 23.5 vs 59.0; K = 14336 6.6 vs 12.5),
+// so AUTO takes it whenever a' >= 32. `rows` is kept for callers that decide for a batch.
 bool rowquant_tc_auto(int ap_tc, int64_t rows) {
-  return ap_tc >= 32 && (rows >= 2048 || (ap_tc > 64 && rows >= 1024));
+  return ap_tc >= 32 && rows >= 1;
 }
 
 template <int MT, int G>

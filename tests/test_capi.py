@@ -136,13 +136,12 @@ def test_host_pipeline_needs_cuda_device():
 
 
 def test_rowquant_auto_tc_rule():
-    """dscq_rowquant_auto_tc (host only): the tcgen05 quantizer from 2048 rows, from 1024 rows when the
-    dense factor a' = K / 64 exceeds 64, never outside 32 <= a' <= 224 or without a Hadamard split."""
+    """dscq_rowquant_auto_tc (host only): the tcgen05 quantizer for any row count when the dense factor
+    a' = K / 64 lies in [32, 224]; never outside that range or without a Hadamard split."""
     from dscquant_b200 import _lib
 
     lib = _lib.load()
-    cases = {(4096, 2048): 1, (4096, 2047): 0, (4096, 1024): 0, (8192, 1024): 1, (8192, 1023): 0,
-             (11008, 2048): 1, (11008, 1024): 1, (14336, 1024): 1, (2048, 4096): 1, (1024, 8192): 0,
-             (28672, 4096): 0, (1000, 4096): 0}
+    cases = {(4096, 2048): 1, (4096, 1): 1, (4096, 1024): 1, (8192, 16): 1, (11008, 1): 1, (14336, 512): 1,
+             (2048, 4096): 1, (1024, 8192): 0, (28672, 4096): 0, (1000, 4096): 0, (4096, 0): 0}
     for (K, rows), want in cases.items():
         assert lib.dscq_rowquant_auto_tc(K, rows) == want, (K, rows)
