@@ -713,7 +713,8 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   // long rows K = a * 1024 with a dense factor a <= 32 (K = 28672: H_28 (x) H_1024)
   const bool klong = rotate && p.rot_a > 1 && p.rot_a <= 32 && log2b == 10 &&
                      (mode == DSCQ_ACT_SYM || mode == DSCQ_WEIGHT_SYM) && x_dtype == DSCQ_BF16 && KP == K &&
-                     aligned(x, 16) && ld_x % 8 == 0;
+                     aligned(x, 16) && ld_x % 8 == 0 && (!packed || (aligned(packed, 4) && ld_packed % 4 == 0)) &&
+                     (!codes || (aligned(codes, 8) && ld_codes % 8 == 0));
   if (klong) {
     using KC = dscq::KronLongCfg;
     cudaError_t e = cudaFuncSetAttribute(dscq::kron_long_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, KC::SMEM);

@@ -10,13 +10,12 @@
 //   * the dense factor goes first, on the exact bf16 inputs, as tensor-core tiles (mma.sync
 //     m16n8k16 bf16 -> fp32): D = H_a^T X. Warp w owns M tile w & 1 (16 output rows i') and the
 //     128-column block w >> 1, i.e. a 16 x 128 tile of D in 16 accumulator fragments;
-//   * the 1024-point WHT along c: bits 0..6 (inside a column block) on the fragments -- bit 0 in
-//     the thread, bits 1..2 across the lanes of a quad (shuffles), bits 3..6 across the fragments;
-//     bits 7..9 (across the eight column blocks) after one exchange through shared memory, where
-//     each thread takes the eight blocks' values of a (row, column pair) and finishes the
-//     transform in registers;
-//   * row absmax over the CTA, then codes and packed bytes straight from those registers (a
-//     column pair is one byte, consecutive threads write consecutive bytes);
+//   * the 1024-point WHT along c (column c = 128 cb + 8 n + 2 q + e): bit 0 (e) inside the thread and
+//     bits 3..6 (n) across its fragments, then one exchange through shared memory after which each
+//     thread holds one (row, n) item -- the 32 column pairs that differ in q and cb -- and finishes
+//     bits 1..2 and 7..9 in registers (no shuffles);
+//   * row absmax over the CTA, then codes from those registers: the four q of one cb are consecutive
+//     bytes, one 32-bit store (and one 8-byte store of int8 codes);
 //   * the next row's cp.async into the input buffer starts as soon as the MMAs have read it.
 #pragma once
 #include "kron_quant.cuh"
@@ -31,7 +30,6 @@ struct KronLongCfg {
   static constexpr int XS_BYTES = ROWS * 2048;       // [32][1024] bf16
   static constexpr int YS_BYTES = 32 * 1024 * 4;     // [<= 32][1024] fp32 exchange
   static constexpr int SMEM = XS_BYTES + YS_BYTES + 128;
-  static constexpr int ITEMS_MAX = 4;                // (row, column pair) items per thread: 32 * 64 / 512
 };
 
 // x rows of K = a * 1024 bf16; p.h_a = H_a ([a, a] +-1, row-major, device memory), 2 <= a <= 32.
@@ -111,9 +109,10 @@ __global__ void __launch_bounds__(KronLongCfg::THREADS, 1) kron_long_quant(const
     __syncthreads();     // every warp has read x: the buffer takes the next row
     issue(row + stride);
 
-    // ---- WHT along the block-local column 8n + 2q + e, bits 0..6
+    // ---- WHT bits 0 (e, inside the thread) and 3..6 (n, across this thread's fragments); bits 1..2 (q, the
+    // quad's lanes) and 7..9 (cb, the column blocks) are done after the exchange, in registers
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {  // bit 0 (e)
+    for (int n = 0; n < 16; ++n) {  // bit 0
       float t0 = acc[n][0], t1 = acc[n][1];
       acc[n][0] = t0 + t1;
       acc[n][1] = t0 - t1;
@@ -123,30 +122,24 @@ __global__ void __launch_bounds__(KronLongCfg::THREADS, 1) kron_long_quant(const
       acc[n][3] = t0 - t1;
     }
 #pragma unroll
-    for (int bit = 1; bit <= 2; bit <<= 1) {  // bits 1, 2 (quad lanes)
-      const float sgn = (q & bit) ? -1.f : 1.f;
-#pragma unroll
-      for (int n = 0; n < 16; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float o = __shfl_xor_sync(0xffffffffu, acc[n][e], bit);
-          acc[n][e] = fmaf(acc[n][e], sgn, o);
-        }
-    }
-#pragma unroll
-    for (int h = 1; h < 16; h <<= 1)  // bits 3..6 (n)
+    for (int h = 1; h < 16; h <<= 1)  // bits 3..6, packed over (e = 0, 1)
 #pragma unroll
       for (int n = 0; n < 16; ++n)
         if (!(n & h)) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float u = acc[n][e], v = acc[n + h][e];
-            acc[n][e] = u + v;
-            acc[n + h][e] = u - v;
+          for (int hf = 0; hf < 2; ++hf) {
+            const float2 u = make_float2(acc[n][2 * hf], acc[n][2 * hf + 1]);
+            const float2 w = make_float2(acc[n + h][2 * hf], acc[n + h][2 * hf + 1]);
+            const float2 s0 = __fadd2_rn(u, w), s1 = __ffma2_rn(w, make_float2(-1.f, -1.f), u);
+            acc[n][2 * hf] = s0.x;
+            acc[n][2 * hf + 1] = s0.y;
+            acc[n + h][2 * hf] = s1.x;
+            acc[n + h][2 * hf + 1] = s1.y;
           }
         }
 
-    // ---- exchange: ys[i][c] as float2 units (c / 2) swizzled by ((i & 7) << 2) within 64-unit blocks
+    // ---- exchange: ys[i][c] as float2 units (c / 2 = 64 cb + 4 n + q), groups of four units permuted by
+    // (i & 7) within each 64-unit block (unit 4 n + q -> 4 (n ^ (i & 7)) + q)
     float2* y2 = reinterpret_cast<float2*>(ys);
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
@@ -161,30 +154,50 @@ __global__ void __launch_bounds__(KronLongCfg::THREADS, 1) kron_long_quant(const
     }
     __syncthreads();
 
-    // ---- bits 7..9: item (i, pair pp) holds columns 128 j + 2 pp + {0, 1}, j = 0..7
-    float2 v[C::ITEMS_MAX][8];
+    // ---- item (i, n) = this thread: the 32 column pairs 128 cb + 8 n + 2 q + {0, 1}, cb = 0..7, q = 0..3,
+    // read as 32-byte groups; WHT bits 1..2 and 7..9 in registers
+    const int it_i = threadIdx.x >> 4, it_n = threadIdx.x & 15;
+    const bool item_live = it_i < a;
+    float2 v[8][4];
     float amax = 0.f;
-    const int items = a * 64;
+    if (item_live) {
+      const float2* src = y2 + it_i * 512 + 4 * (it_n ^ (it_i & 7));
 #pragma unroll
-    for (int t = 0; t < C::ITEMS_MAX; ++t) {
-      const int item = threadIdx.x + t * C::THREADS;
-      if (item < items) {
-        const int i = item >> 6, pp = item & 63;
-        const int su = pp ^ ((i & 7) << 2);
+      for (int c = 0; c < 8; ++c) {
+        const float4 g0 = *reinterpret_cast<const float4*>(src + c * 64);
+        const float4 g1 = *reinterpret_cast<const float4*>(src + c * 64 + 2);
+        v[c][0] = make_float2(g0.x, g0.y);
+        v[c][1] = make_float2(g0.z, g0.w);
+        v[c][2] = make_float2(g1.x, g1.y);
+        v[c][3] = make_float2(g1.z, g1.w);
+      }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[t][j] = y2[i * 512 + j * 64 + su];
+      for (int hq = 1; hq < 4; hq <<= 1)  // bits 1..2
 #pragma unroll
-        for (int h = 1; h < 8; h <<= 1)
+        for (int c = 0; c < 8; ++c)
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (!(j & h)) {
-              const float2 x0 = v[t][j], x1 = v[t][j + h];
-              v[t][j] = __fadd2_rn(x0, x1);
-              v[t][j + h] = __ffma2_rn(x1, make_float2(-1.f, -1.f), x0);
+          for (int qq = 0; qq < 4; ++qq)
+            if (!(qq & hq)) {
+              const float2 u = v[c][qq], w = v[c][qq + hq];
+              v[c][qq] = __fadd2_rn(u, w);
+              v[c][qq + hq] = __ffma2_rn(w, make_float2(-1.f, -1.f), u);
             }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fmaxf(fabsf(v[t][j].x), fabsf(v[t][j].y)));
-      }
+      for (int hc = 1; hc < 8; hc <<= 1)  // bits 7..9
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          if (!(c & hc)) {
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+              const float2 u = v[c][qq], w = v[c + hc][qq];
+              v[c][qq] = __fadd2_rn(u, w);
+              v[c + hc][qq] = __ffma2_rn(w, make_float2(-1.f, -1.f), u);
+            }
+          }
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) amax = fmaxf(amax, fmaxf(fabsf(v[c][qq].x), fabsf(v[c][qq].y)));
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -198,34 +211,36 @@ __global__ void __launch_bounds__(KronLongCfg::THREADS, 1) kron_long_quant(const
     const float scale = fmaxf(__fdiv_rn(__fmul_rn(amax_y, p.clip), 7.f), 1e-8f);
     const float cm = __fdiv_rn(p.norm, scale);
 
-    // ---- codes: column pair (128 j + 2 pp, +1) of row i is byte i * 512 + 64 j + pp
+    // ---- codes: column pair (128 cb + 8 n + 2 q, +1) of row i is byte i * 512 + 64 cb + 4 n + q, so the
+    // four q of one cb are one 32-bit word (and eight consecutive int8 codes)
     uint8_t* prow = p.packed ? p.packed + static_cast<int64_t>(row) * p.ld_packed : nullptr;
     int8_t* crow = p.codes ? p.codes + static_cast<int64_t>(row) * p.ld_codes : nullptr;
     int csum = 0;
+    if (item_live) {
+      const float2 cm2 = make_float2(cm, cm), magic = make_float2(12582912.f, 12582912.f);
 #pragma unroll
-    for (int t = 0; t < C::ITEMS_MAX; ++t) {
-      const int item = threadIdx.x + t * C::THREADS;
-      if (item < items) {
-        const int i = item >> 6, pp = item & 63;
+      for (int c = 0; c < 8; ++c) {
+        uint32_t word = 0, lo8 = 0, hi8 = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float q0 = v[t][j].x * cm, q1 = v[t][j].y * cm;
+        for (int qq = 0; qq < 4; ++qq) {
+          float2 qv = __fmul2_rn(v[c][qq], cm2);
           if (clamp) {
-            q0 = fminf(fmaxf(q0, lo), 7.f);
-            q1 = fminf(fmaxf(q1, lo), 7.f);
+            qv.x = fminf(fmaxf(qv.x, lo), 7.f);
+            qv.y = fminf(fmaxf(qv.y, lo), 7.f);
           }
-          const uint32_t c0 = __float_as_uint(q0 + 12582912.f) & 15u;
-          const uint32_t c1 = __float_as_uint(q1 + 12582912.f) & 15u;
-          if (prow) prow[i * 512 + j * 64 + pp] = static_cast<uint8_t>(c0 | (c1 << 4));
+          const float2 r = __fadd2_rn(qv, magic);
+          const uint32_t c0 = __float_as_uint(r.x) & 15u, c1 = __float_as_uint(r.y) & 15u;
+          word |= (c0 | (c1 << 4)) << (8 * qq);
           if (crow || p.row_sums) {
             const int s0 = static_cast<int>(c0 << 28) >> 28, s1 = static_cast<int>(c1 << 28) >> 28;
             csum += s0 + s1;
-            if (crow) {
-              crow[i * 1024 + j * 128 + 2 * pp] = static_cast<int8_t>(s0);
-              crow[i * 1024 + j * 128 + 2 * pp + 1] = static_cast<int8_t>(s1);
-            }
+            const uint32_t pr = (static_cast<uint32_t>(s0) & 0xFFu) | ((static_cast<uint32_t>(s1) & 0xFFu) << 8);
+            if (qq < 2) lo8 |= pr << (16 * qq);
+            else hi8 |= pr << (16 * (qq - 2));
           }
         }
+        if (prow) *reinterpret_cast<uint32_t*>(prow + it_i * 512 + c * 64 + 4 * it_n) = word;
+        if (crow) *reinterpret_cast<uint2*>(crow + it_i * 1024 + c * 128 + 8 * it_n) = make_uint2(lo8, hi8);
       }
     }
     if (p.row_sums) {
