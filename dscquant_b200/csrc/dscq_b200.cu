@@ -302,7 +302,7 @@ cudaError_t launch_rotq(const CUtensorMap& tm, const dscq::RotqParams& rp, cudaS
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const int grid = std::min(rp.groups, num_sms());
-  const int nwarps = std::max(rp.tma_warp, rp.mma_warp) + 1;
+  const int nwarps = std::max(std::max(rp.tma_warp, rp.mma_warp), rp.mma_warp2) + 1;
   const int threads = std::max(nwarps, (rp.nteam - 1) * rp.team_stride + rp.tw) * 32;
   if (threads > dscq::RqThreads<MT, G>::value) return cudaErrorInvalidConfiguration;
   dscq::rotq_tc<MT, G><<<grid, threads, smem, st>>>(tm, rp);
@@ -664,12 +664,14 @@ int dscq_rowquant_variant(const void* x, int x_dtype, int64_t M, int64_t K, int6
       rp.nteam = 4;
       rp.tma_warp = 16;
       rp.mma_warp = 17;
+      rp.mma_warp2 = -1;
     } else {  // two teams of 4 + ceil((a' - 128) / 32) warps at warps 0.. and 8..
       rp.tw = 4 + (rp.ap - 128 + 31) / 32;
       rp.team_stride = 8;
       rp.nteam = 2;
       rp.tma_warp = rp.tw <= 6 ? 6 : (rp.tw == 7 ? 7 : 16);
       rp.mma_warp = rp.tw <= 6 ? 7 : (rp.tw == 7 ? 15 : 17);
+      rp.mma_warp2 = rp.tw <= 6 ? 15 : -1;  // warp 15 is free when each team has at most 6 warps
     }
     if (rp.ns < 2) return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize: shared memory too small");
     int dev = 0;
@@ -1188,12 +1190,14 @@ extern "C" int dscq_rowquant_tc_noalloc(const void* x, int x_dtype, int64_t M, i
     rp.nteam = 4;
     rp.tma_warp = 16;
     rp.mma_warp = 17;
+    rp.mma_warp2 = -1;
   } else {
     rp.tw = 4 + (rp.ap - 128 + 31) / 32;
     rp.team_stride = 8;
     rp.nteam = 2;
     rp.tma_warp = rp.tw <= 6 ? 6 : (rp.tw == 7 ? 7 : 16);
     rp.mma_warp = rp.tw <= 6 ? 7 : (rp.tw == 7 ? 15 : 17);
+    rp.mma_warp2 = rp.tw <= 6 ? 15 : -1;
   }
   if (rp.ns < 2) return fail(DSCQ_ERR_UNSUPPORTED, "tcgen05 rotate+quantize: shared memory too small");
   if (rp.a_bytes > kRotqScratchBytes)

@@ -60,6 +60,7 @@ struct RotqParams {
   int tw;                // warps per team
   int team_stride;       // team t owns warps [t * team_stride, t * team_stride + tw)
   int tma_warp, mma_warp;
+  int mma_warp2;         // two M tiles: a second MMA issuer taking M tile 1 (-1: mma_warp issues both)
   int split;             // 1: every team takes one block of each MMA group; 0: teams take whole groups
   const uint8_t* a_op;   // global image of the A operand (a_bytes, 16-byte aligned), rotq_build_operand
 };
@@ -270,13 +271,13 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
     tma_prefetch_desc(&tmX);
     for (int s = 0; s < ns; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], rp.mma_warp2 >= 0 ? 2 : 1);  // one commit per MMA issuer
     }
     for (int s = 0; s < S; ++s) {
-      mbar_init(&tfull[s], 1);
+      mbar_init(&tfull[s], rp.mma_warp2 >= 0 ? 2 : 1);
       mbar_init(&tempty[s], rp.split ? tw * rp.nteam : tw);
     }
-    mbar_init(done, 1);
+    mbar_init(done, rp.mma_warp2 >= 0 ? 2 : 1);
     mbar_init(aready, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -318,8 +319,10 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
         for (int j = n > ns ? n - ns : 0; j < n; ++j) mbar_wait(&full[j % ns], (j / ns) & 1u, nullptr);
       }
     }
-  } else if (warp == rp.mma_warp) {
-    // ------------------------------------------------ MMA issuer: groups of G token blocks
+  } else if (warp == rp.mma_warp || warp == rp.mma_warp2) {
+    // ------------------------------------------------ MMA issuer(s): groups of G token blocks. Each
+    // tcgen05.mma costs the issuing thread ~110 cycles whatever N, so with two M tiles (22 MMAs per
+    // group at a' = 172) a second issuer takes M tile 1: K = 11008 at 2048 rows 25.6 -> 24.0 us.
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16_bmn(128, 64 * G);
       const uint32_t a0 = smem_u32(a_base);
@@ -332,8 +335,9 @@ __global__ void __launch_bounds__(RqThreads<MT, G>::value, 1)
         if (!ok) break;
         tc_fence_after();
         const uint32_t b0 = smem_u32(b_base + (n0 % ns) * rp.stage_bytes);  // ns % G == 0: contiguous stages
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
+        const int m_lo = warp == rp.mma_warp2 ? 1 : 0;
+        const int m_hi = rp.mma_warp2 >= 0 ? m_lo + 1 : MT;
+        for (int m = m_lo; m < m_hi; ++m) {
           const uint32_t d = tmem_base + static_cast<uint32_t>(slot * SLOT + m * 64 * G);
           for (int ks = 0; ks < rp.ksteps; ++ks) {
             const uint64_t ad = umma_desc_sw128(a0 + (m * rp.nkb + (ks >> 2)) * 16384 + (ks & 3) * 32);
