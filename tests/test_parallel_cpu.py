@@ -87,3 +87,18 @@ def test_row_bounds_cover_all_rows():
             assert spans[0][0] == 0 and spans[-1][1] == M
             assert all(lo <= hi for lo, hi in spans)
             assert all(spans[r][1] == spans[r + 1][0] for r in range(world - 1))
+
+
+def test_exchange_mode_resolution():
+    """'auto' takes the epilogue stores up to 2 GPUs and the pushed row blocks from 3 (measured on B200);
+    explicit modes pass through; anything else is rejected."""
+    from dscquant_b200 import parallel
+
+    assert parallel.resolve_mode("auto", 1) == "fused"
+    assert parallel.resolve_mode("auto", 2) == "fused"
+    assert parallel.resolve_mode("auto", 4) == "push"
+    assert parallel.resolve_mode("auto", 8) == "push"
+    for m in ("fused", "push", "nccl"):
+        assert parallel.resolve_mode(m, 8) == m
+    with pytest.raises(ValueError):
+        parallel.resolve_mode("allgather", 2)
